@@ -1,0 +1,31 @@
+// Library context behind the opaque sgblasHandle_t.
+//
+// Mirrors the reference's two-field context (src/handle_internal.hpp:6-9 of
+// AG0708/sgBLAS: stream + math mode) and adds the device workspace used by
+// the split-K reduction, which the reference does not have. The workspace is
+// grow-only, owned by the context, allocated stream-ordered on the handle's
+// stream and released in sgblasDestroy.
+#ifndef SGBLAS_B200_CONTEXT_HPP_
+#define SGBLAS_B200_CONTEXT_HPP_
+
+#include <sgblas/sgblas.h>
+
+#include <cstddef>
+
+struct sgblasContext {
+  sgblasStream_t stream = nullptr;
+  sgblasMathMode_t math_mode = SGBLAS_MATH_FP32;
+
+  // Split-K partial sums (FP32). device == -1 means nothing allocated.
+  void *workspace = nullptr;
+  std::size_t workspace_bytes = 0;
+  int workspace_device = -1;
+};
+
+namespace sgblas::detail {
+// Releases the context's device workspace (defined with the CUDA code; a
+// no-op when nothing was allocated).
+void releaseWorkspace(sgblasContext *context);
+}  // namespace sgblas::detail
+
+#endif  // SGBLAS_B200_CONTEXT_HPP_

@@ -1,0 +1,97 @@
+// Thin inline-PTX wrappers for sm_100a: mbarriers, TMA tile loads, cp.async.
+//
+// Every wait on an mbarrier is bounded (kSpinLimit polls of try_wait, each of
+// which itself suspends for a hardware-defined slice); a wait that runs out
+// records an error code in the library's device error word and returns false,
+// so that a kernel never spins forever on a copy that did not arrive.
+#ifndef SGBLAS_B200_PTX_CUH_
+#define SGBLAS_B200_PTX_CUH_
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace sgblas::kern {
+
+// Poll budget of one bounded mbarrier wait (each try_wait suspends the
+// thread for up to a hardware time slice, so this is well above a second).
+constexpr uint32_t kSpinLimit = 1u << 24;
+
+// Device error word codes (OR-ed together).
+constexpr unsigned kErrBarrierTimeout = 1u;
+
+__device__ __forceinline__ uint32_t smemAddr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbarInit(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smemAddr(bar)), "r"(count)
+               : "memory");
+}
+
+// Makes mbarrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fenceBarrierInit() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbarArriveExpectTx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smemAddr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbarTryWait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smemAddr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete.
+__device__ __forceinline__ bool mbarWait(uint64_t *bar, uint32_t parity, unsigned *err) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbarTryWait(bar, parity)) return true;
+  }
+  if (err != nullptr) atomicOr(err, kErrBarrierTimeout);
+  return false;
+}
+
+// 2-D TMA tile load global -> shared, completion signalled on `bar`.
+// x is the innermost (contiguous) coordinate in elements.
+__device__ __forceinline__ void tmaLoad2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x,
+                                          int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smemAddr(dst)),
+      "l"(map), "r"(smemAddr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetchTensorMap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// 4-byte cp.async with zero fill: copies `bytes` (0 or 4) and zero-fills the
+// rest of the 4-byte destination, so a predicated-off element reads as 0.
+__device__ __forceinline__ void cpAsync4(void *dst, const void *src, uint32_t bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smemAddr(dst)), "l"(src),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void cpAsyncCommit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cpAsyncWait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+}  // namespace sgblas::kern
+
+#endif  // SGBLAS_B200_PTX_CUH_

@@ -1,0 +1,374 @@
+// The strict-FP32 tile kernel: C tile += op(A) panel * op(B) panel on CUDA
+// cores with the sm_100 packed FP32 FMA (FFMA2, fma.rn.f32x2).
+//
+// Replaces the reference's SIMT FFMA kernels (src/sgemm_cuda.cu:86-395 and
+// src/sgemm_async_sm80*.cu of AG0708/sgBLAS) with one family covering all four
+// transpose modes, tails and any leading dimension.
+//
+// Arithmetic. Each FFMA2 performs two independent IEEE fma.rn operations, so
+// every output is a chain of FP32 fused multiply-adds in k order -- the
+// arithmetic of the reference's fmaf loops (no TF32, no tensor cores). The
+// epilogue is the reference's: p = alpha*acc; beta == 0: c = p; beta == 1:
+// c = c + p; otherwise c = fmaf(beta, c, p) (src/sgemm_cuda.cu:116-123).
+//
+// Operand roles. FFMA2 multiplies a register pair by a register pair. The
+// "pair" operand P feeds two elements adjacent along its free dimension (half
+// of a 16-byte shared-memory load); the "broadcast" operand D feeds one element
+// to both lanes. P must sit in shared memory as [k][x] (x contiguous); D may be
+// [k][x] or [x][k].
+//
+// Shared-memory tile layouts (a pipeline stage holds one P and one D tile):
+//   kXK : [BK][BX] floats, x contiguous -- what TMA writes when x is the
+//         contiguous global dimension.
+//   kKX : [BX][BK] floats, k contiguous, 64-byte rows with the TMA 64B swizzle
+//         (16-byte chunk index ^= (row >> 1) & 3).
+//
+// CTA tile: 256 (P) x 128 (D), 256 threads = 8 warps, one CTA per SM; each
+// thread owns a 16 (P) x 8 (D) block of C (64 FFMA2 per k step against 4+2
+// shared loads). Warps form 2 (P) x 4 (D); lane bits lp = lane % 8,
+// ld = lane / 8.
+//   P coordinates: 128*wp + 4*lp + {0..3} + 32*q, q = 0..3.
+//   D coordinates, kXK D tile: 32*wd + 4*ld + {0..3} + {0, 16}.
+//   D coordinates, kKX D tile: 64*(wd/2) + 4*(wd%2) + ld + 8*j, j = 0..7 --
+//     all eight rows of a thread share one swizzle phase ((row >> 1) & 3), and
+//     the four rows a warp reads together fall in four distinct bank groups.
+#ifndef SGBLAS_B200_SGEMM_TILE_CUH_
+#define SGBLAS_B200_SGEMM_TILE_CUH_
+
+#include "ptx.cuh"
+
+#include <cstddef>
+#include <cstdint>
+
+namespace sgblas::kern {
+
+constexpr int kBP = 256;   // pair-operand tile extent
+constexpr int kBD = 128;   // broadcast-operand tile extent
+constexpr int kBK = 16;    // k slice per pipeline stage
+constexpr int kStages = 6;
+constexpr int kThreads = 256;
+constexpr int kTP = 16;    // pair-operand elements per thread
+constexpr int kTD = 8;     // broadcast-operand elements per thread
+constexpr int kPairFloats = kBP * kBK;
+constexpr int kDupFloats = kBD * kBK;
+constexpr int kPairBytes = kPairFloats * 4;   // 16 KiB
+constexpr int kDupBytes = kDupFloats * 4;     // 8 KiB
+constexpr int kStageBytes = kPairBytes + kDupBytes;
+constexpr int kSmemAlign = 1024;
+constexpr int kSmemBytes = kStages * kStageBytes + 256 + kSmemAlign;
+
+enum class Beta { kZero, kOne, kGeneral };
+enum class Src { kTma, kCopy };
+enum class Layout { kXK, kKX };
+
+struct GemmParams {
+  CUtensorMap tma_a;  // valid when the kernel stages tiles with TMA
+  CUtensorMap tma_b;
+  const float *a;
+  const float *b;
+  float *c;
+  int m, n, k;
+  int lda, ldb, ldc;
+  float alpha, beta;
+  int tiles_m, tiles_n;
+  int group_m;        // raster: tile rows per CTA group
+  unsigned *err;      // device error word
+};
+
+// Byte offset of element (x, k) inside a kKX tile.
+__device__ __forceinline__ uint32_t kxOffset(int x, int k) {
+  return static_cast<uint32_t>(x * 64 + ((((k >> 2) ^ (x >> 1)) & 3) << 4) + ((k & 3) << 2));
+}
+
+// Which operand plays which role, and the tile shape that follows.
+template <bool kTA, bool kTB, Src kSrc>
+struct Plan {
+  // Shared-memory layout of each operand. The cp.async path may transpose A
+  // while staging it, so it always stages A as [k][m].
+  static constexpr Layout kA = (kSrc == Src::kTma && kTA) ? Layout::kKX : Layout::kXK;
+  static constexpr Layout kB = kTB ? Layout::kXK : Layout::kKX;
+  static constexpr bool kPairIsA = (kA == Layout::kXK);
+  static constexpr Layout kD = kPairIsA ? kB : kA;
+  static_assert(kPairIsA || kB == Layout::kXK, "one operand must be staged as [k][x]");
+  static constexpr int kBM = kPairIsA ? kBP : kBD;
+  static constexpr int kBN = kPairIsA ? kBD : kBP;
+};
+
+// Tile index -> (tile_m, tile_n): groups of group_m tile rows are walked
+// column by column so that concurrently running CTAs share panels in L2.
+__device__ __forceinline__ void rasterTile(const GemmParams &p, int t, int *tm, int *tn) {
+  const int per_group = p.group_m * p.tiles_n;
+  const int group = t / per_group;
+  const int first = group * p.group_m;
+  const int rows = min(p.tiles_m - first, p.group_m);
+  const int in = t - group * per_group;
+  *tm = first + in % rows;
+  *tn = in / rows;
+}
+
+// ---- cp.async staging (any alignment, any leading dimension, tails) --------
+// Writes the layouts the kernel reads: A as [k][m] (P, kBP wide), B as [k][n]
+// or swizzled [n][k] (D, kBD wide), zero-filled outside the matrix. Global
+// reads are coalesced along each operand's contiguous dimension.
+template <bool kTA, bool kTB>
+__device__ __forceinline__ void copyTile(const GemmParams &p, float *sa, float *sb, int m0, int n0,
+                                         int k0) {
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int r = 0; r < kPairFloats / kThreads; ++r) {
+    const int e = tid + r * kThreads;
+    const int mm = kTA ? e / kBK : e % kBP;
+    const int kk = kTA ? e % kBK : e / kBP;
+    const int gm = m0 + mm, gk = k0 + kk;
+    const bool ok = gm < p.m && gk < p.k;
+    const float *src = p.a;
+    if (ok) {
+      src = kTA ? p.a + static_cast<size_t>(gk) + static_cast<size_t>(gm) * p.lda
+                : p.a + static_cast<size_t>(gm) + static_cast<size_t>(gk) * p.lda;
+    }
+    cpAsync4(sa + kk * kBP + mm, src, ok ? 4u : 0u);
+  }
+#pragma unroll
+  for (int r = 0; r < kDupFloats / kThreads; ++r) {
+    const int e = tid + r * kThreads;
+    const int nn = kTB ? e % kBD : e / kBK;
+    const int kk = kTB ? e / kBD : e % kBK;
+    const int gn = n0 + nn, gk = k0 + kk;
+    const bool ok = gn < p.n && gk < p.k;
+    const float *src = p.b;
+    if (ok) {
+      src = kTB ? p.b + static_cast<size_t>(gn) + static_cast<size_t>(gk) * p.ldb
+                : p.b + static_cast<size_t>(gk) + static_cast<size_t>(gn) * p.ldb;
+    }
+    float *dst = kTB ? sb + kk * kBD + nn
+                     : reinterpret_cast<float *>(reinterpret_cast<char *>(sb) + kxOffset(nn, kk));
+    cpAsync4(dst, src, ok ? 4u : 0u);
+  }
+}
+
+// Per-thread addressing of the broadcast tile.
+struct DupAddr {
+  uint32_t base;        // kXK: float index of the first column; kKX: byte offset of row 0
+  uint32_t chunk[4];    // kKX: swizzled byte offset of each 16-byte k chunk
+};
+
+// ---- the FFMA2 micro-kernel over one BK slice ------------------------------
+template <Layout kD>
+__device__ __forceinline__ void computeStage(const float *sp, const float *sd, int p_base,
+                                             const DupAddr &da, float2 (&acc)[kTP / 2][kTD]) {
+#pragma unroll
+  for (int k = 0; k < kBK; k += 2) {
+    float dv[2][kTD];
+    if constexpr (kD == Layout::kXK) {
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const float4 d0 = *reinterpret_cast<const float4 *>(sd + (k + kk) * kBD + da.base);
+        const float4 d1 = *reinterpret_cast<const float4 *>(sd + (k + kk) * kBD + da.base + 16);
+        dv[kk][0] = d0.x; dv[kk][1] = d0.y; dv[kk][2] = d0.z; dv[kk][3] = d0.w;
+        dv[kk][4] = d1.x; dv[kk][5] = d1.y; dv[kk][6] = d1.z; dv[kk][7] = d1.w;
+      }
+    } else {
+      const char *row0 = reinterpret_cast<const char *>(sd) + da.base + da.chunk[k >> 2] +
+                         ((k & 3) << 2);
+#pragma unroll
+      for (int j = 0; j < kTD; ++j) {
+        const float2 v = *reinterpret_cast<const float2 *>(row0 + 512 * j);
+        dv[0][j] = v.x;
+        dv[1][j] = v.y;
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      float2 pv[kTP / 2];
+#pragma unroll
+      for (int q = 0; q < kTP / 4; ++q) {
+        const float4 v = *reinterpret_cast<const float4 *>(sp + (k + kk) * kBP + p_base + 32 * q);
+        pv[2 * q] = make_float2(v.x, v.y);
+        pv[2 * q + 1] = make_float2(v.z, v.w);
+      }
+#pragma unroll
+      for (int i = 0; i < kTP / 2; ++i) {
+#pragma unroll
+        for (int j = 0; j < kTD; ++j) {
+          acc[i][j] = __ffma2_rn(pv[i], make_float2(dv[kk][j], dv[kk][j]), acc[i][j]);
+        }
+      }
+    }
+  }
+}
+
+template <Beta kBeta>
+__device__ __forceinline__ float epilogueValue(float acc, float alpha, float beta, float c) {
+  const float prod = alpha * acc;
+  if constexpr (kBeta == Beta::kZero) {
+    return prod;
+  } else if constexpr (kBeta == Beta::kOne) {
+    return c + prod;
+  } else {
+    return fmaf(beta, c, prod);
+  }
+}
+
+// ---- the kernel: one tile of C per CTA --------------------------------------
+template <bool kTA, bool kTB, Beta kBeta, Src kSrc>
+__global__ void __launch_bounds__(kThreads, 1) sgemmTileKernel(const __grid_constant__ GemmParams p) {
+  using P = Plan<kTA, kTB, kSrc>;
+  extern __shared__ unsigned char smem_raw[];
+  // Align within the shared window by offsetting smem_raw itself: pointers
+  // derived from the __shared__ array stay in the shared address space, so the
+  // compiler emits 32-bit shared loads (a uintptr_t round trip would turn them
+  // into 64-bit generic loads and double the address registers).
+  unsigned char *smem = smem_raw + ((kSmemAlign - (smemAddr(smem_raw) & (kSmemAlign - 1))) &
+                                    (kSmemAlign - 1));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+  // Stage s: the pair tile at offset 0, the broadcast tile after it.
+  auto stageP = [&](int s) { return reinterpret_cast<float *>(smem + s * kStageBytes); };
+  auto stageD = [&](int s) {
+    return reinterpret_cast<float *>(smem + s * kStageBytes + kPairBytes);
+  };
+  auto stageA = [&](int s) { return P::kPairIsA ? stageP(s) : stageD(s); };
+  auto stageB = [&](int s) { return P::kPairIsA ? stageD(s) : stageP(s); };
+
+  int tile_m, tile_n;
+  rasterTile(p, blockIdx.x, &tile_m, &tile_n);
+  const int m0 = tile_m * P::kBM, n0 = tile_n * P::kBN;
+  const int kiters = (p.k + kBK - 1) / kBK;
+
+  const int tid = threadIdx.x;
+  const int warp = tid / 32, lane = tid % 32;
+  const int wp = warp % 2, wd = warp / 2;
+  const int lp = lane % 8, ld = lane / 8;
+  const int p_base = wp * 128 + lp * 4;
+  DupAddr da;
+  int d_row0;  // kKX: first row; kXK: first column
+  if constexpr (P::kD == Layout::kXK) {
+    d_row0 = wd * 32 + ld * 4;
+    da.base = static_cast<uint32_t>(d_row0);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) da.chunk[c] = 0;
+  } else {
+    d_row0 = (wd / 2) * 64 + (wd % 2) * 4 + ld;
+    da.base = static_cast<uint32_t>(d_row0 * 64);
+    const int phase = (d_row0 >> 1) & 3;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) da.chunk[c] = static_cast<uint32_t>((c ^ phase) << 4);
+  }
+  auto dCoord = [&](int j) {
+    return P::kD == Layout::kXK ? d_row0 + (j & 3) + 16 * (j >> 2) : d_row0 + 8 * j;
+  };
+  auto pCoord = [&](int i) { return p_base + (i & 3) + 32 * (i >> 2); };
+
+  if constexpr (kSrc == Src::kTma) {
+    if (tid == 0) {
+      prefetchTensorMap(&p.tma_a);
+      prefetchTensorMap(&p.tma_b);
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) mbarInit(&full[s], 1);
+      fenceBarrierInit();
+    }
+    __syncthreads();
+  }
+
+  auto issue = [&](int kt) {
+    const int s = kt % kStages;
+    const int k0 = kt * kBK;
+    if constexpr (kSrc == Src::kTma) {
+      mbarArriveExpectTx(&full[s], kStageBytes);
+      if (P::kA == Layout::kXK) tmaLoad2d(stageA(s), &p.tma_a, &full[s], m0, k0);
+      else tmaLoad2d(stageA(s), &p.tma_a, &full[s], k0, m0);
+      if (P::kB == Layout::kXK) tmaLoad2d(stageB(s), &p.tma_b, &full[s], n0, k0);
+      else tmaLoad2d(stageB(s), &p.tma_b, &full[s], k0, n0);
+    } else {
+      copyTile<kTA, kTB>(p, stageA(s), stageB(s), m0, n0, k0);
+    }
+  };
+
+  // Prologue: fill kStages-1 stages.
+  if constexpr (kSrc == Src::kTma) {
+    if (tid == 0) {
+      for (int kt = 0; kt < kStages - 1 && kt < kiters; ++kt) issue(kt);
+    }
+  } else {
+#pragma unroll
+    for (int kt = 0; kt < kStages - 1; ++kt) {
+      if (kt < kiters) issue(kt);
+      cpAsyncCommit();
+    }
+  }
+
+  float2 acc[kTP / 2][kTD];
+#pragma unroll
+  for (int i = 0; i < kTP / 2; ++i)
+#pragma unroll
+    for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
+
+  bool alive = true;
+  for (int kt = 0; kt < kiters; ++kt) {
+    const int s = kt % kStages;
+    if constexpr (kSrc == Src::kTma) {
+      const bool landed = mbarWait(&full[s], (kt / kStages) & 1, p.err);
+      // The barrier doubles as a vote, so that a timed-out wait stops the
+      // whole CTA together instead of stranding the others at a barrier; it
+      // also means every warp is done with tile kt-1, whose stage is free.
+      if (!__syncthreads_and(landed)) {
+        alive = false;
+        break;
+      }
+      if (tid == 0 && kt + kStages - 1 < kiters) issue(kt + kStages - 1);
+    } else {
+      cpAsyncWait<kStages - 2>();
+      __syncthreads();
+      if (kt + kStages - 1 < kiters) issue(kt + kStages - 1);
+      cpAsyncCommit();
+    }
+    computeStage<P::kD>(stageP(s), stageD(s), p_base, da, acc);
+  }
+  if constexpr (kSrc == Src::kCopy) cpAsyncWait<0>();
+  if (!alive) return;
+
+  // ---- epilogue ----
+  // Element (i, j) of the thread's block: pair coordinate pCoord(i), i = 0..15,
+  // broadcast coordinate dCoord(j), j = 0..7; acc[i/2][j] holds (i even, i odd).
+  const float alpha = p.alpha, beta = p.beta;
+  if constexpr (P::kPairIsA) {
+    const bool vec = m0 + P::kBM <= p.m && n0 + P::kBN <= p.n && (p.ldc % 4 == 0) &&
+                     (reinterpret_cast<uintptr_t>(p.c) % 16 == 0);
+    if (vec) {
+#pragma unroll
+      for (int j = 0; j < kTD; ++j) {
+        float *col = p.c + static_cast<size_t>(n0 + dCoord(j)) * p.ldc + m0 + p_base;
+#pragma unroll
+        for (int q = 0; q < kTP / 4; ++q) {
+          const float2 lo = acc[2 * q][j], hi = acc[2 * q + 1][j];
+          float4 cv = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+          if constexpr (kBeta != Beta::kZero) cv = *reinterpret_cast<const float4 *>(col + 32 * q);
+          float4 out;
+          out.x = epilogueValue<kBeta>(lo.x, alpha, beta, cv.x);
+          out.y = epilogueValue<kBeta>(lo.y, alpha, beta, cv.y);
+          out.z = epilogueValue<kBeta>(hi.x, alpha, beta, cv.z);
+          out.w = epilogueValue<kBeta>(hi.y, alpha, beta, cv.w);
+          *reinterpret_cast<float4 *>(col + 32 * q) = out;
+        }
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kTD; ++j) {
+#pragma unroll
+    for (int i = 0; i < kTP; ++i) {
+      const int row = P::kPairIsA ? m0 + pCoord(i) : m0 + dCoord(j);
+      const int col = P::kPairIsA ? n0 + dCoord(j) : n0 + pCoord(i);
+      if (row < p.m && col < p.n) {
+        float *cp = p.c + static_cast<size_t>(col) * p.ldc + row;
+        const float a = (i & 1) ? acc[i >> 1][j].y : acc[i >> 1][j].x;
+        const float cv = kBeta == Beta::kZero ? 0.0F : *cp;
+        *cp = epilogueValue<kBeta>(a, alpha, beta, cv);
+      }
+    }
+  }
+}
+
+}  // namespace sgblas::kern
+
+#endif  // SGBLAS_B200_SGEMM_TILE_CUH_

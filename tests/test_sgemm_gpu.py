@@ -1,0 +1,181 @@
+"""GPU parity of sgblasSgemm (through the C ABI) against the CPU oracle.
+
+Covers the reference's whole device correctness suite with its exact inputs
+(tests/cuda/correctness.cu:450-647 of AG0708/sgBLAS: 11 products, 3 scale
+cases, 10 null-pointer no-ops), the BASELINE configurations, every loader path
+(TMA and cp.async) in every transpose mode with tails, odd leading dimensions
+and misaligned pointers, and run-to-run determinism.
+
+Bounds: every checked entry must satisfy the north-star bound
+|C - C_ref| <= 2*max(K,2)*2^-24*(|alpha| sum|a b| + |beta c|) (and therefore the
+reference's looser 2e-6 + 8*eps*(K+1)*max(mag,1)); padding rows [m, ldc) must
+be bit-identical; beta == 0 must overwrite NaN-poisoned C.
+"""
+import numpy as np
+import pytest
+
+import sgblas_b200 as sg
+from tests import cases as C
+from tests.gpu_util import check_full, check_sampled, run_sgemm, to_device
+
+pytestmark = pytest.mark.gpu
+
+
+def _assert(res, name):
+    assert res["ok_north_star"] and res["ok_reference"], (name, res)
+    if "padding_ok" in res:
+        assert res["padding_ok"], (name, "padding overwritten")
+
+
+# ---- the reference suite, with its exact inputs -------------------------------
+def test_reference_suite(cuda, handle):
+    torch = cuda
+    stream = torch.cuda.Stream()   # the suite runs on a non-default stream
+    for item in C.reference_suite():
+        if item[0] == "scale":
+            _, name, k, alpha, beta, c0 = item
+            case = C.Case(name, 0, 0, 7, 5, k, 11, max(1, k + 3), 10, alpha, beta)
+            status, out = run_sgemm(torch, handle, case, np.zeros(1, np.float32),
+                                    np.zeros(1, np.float32), c0, stream=stream)
+            assert status == 0, name
+            want = np.zeros((7, 5)) if beta == 0 else beta * c0.reshape(5, 10).T[:7, :].astype(np.float64)
+            got = out.reshape(5, 10).T[:7, :]
+            assert np.all(np.isfinite(got))
+            assert np.all(np.abs(got - want) <= 2 * 2.0 ** -23 * np.maximum(np.abs(want), 1.0)), name
+            assert np.array_equal(out.reshape(5, 10).T[7:, :], c0.reshape(5, 10).T[7:, :]), name
+        else:
+            _, case, a, b, c0 = item
+            status, out = run_sgemm(torch, handle, case, a, b, c0, stream=stream)
+            assert status == 0, case.name
+            _assert(check_full(case, a, b, c0, out), case.name)
+    assert sg.get_device_errors() == 0
+
+
+def test_null_pointer_noops_never_touch_memory(cuda, handle):
+    torch = cuda
+    for ta in (0, 1):
+        for tb in (0, 1):
+            for m, n in ((0, 7), (7, 0)):
+                k = 5
+                lda = max(1, m if ta == 0 else k)
+                ldb = max(1, k if tb == 0 else n)
+                assert handle.sgemm_status(ta, tb, m, n, k, None, None, lda, None, ldb, None, None,
+                                           max(1, m)) == 0
+    assert handle.sgemm_status(0, 0, 7, 5, 9, 0.0, None, 7, None, 9, 1.0, None, 7) == 0
+    assert handle.sgemm_status(0, 0, 7, 5, 0, 2.0, None, 7, None, 1, 1.0, None, 7) == 0
+    torch.cuda.synchronize()   # an accidental launch on NULL would fault here
+
+
+# ---- BASELINE configurations --------------------------------------------------
+def test_cfg1_256_full(cuda, handle):
+    case = C.cfg1()
+    a, b, c = C.cfg_inputs(case, 0, -1)
+    status, out = run_sgemm(cuda, handle, case, a, b, c)
+    assert status == 0
+    _assert(check_full(case, a, b, c, out), case.name)
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_cfg3_transpose_tail_sweep(cuda, handle, ta, tb):
+    torch = cuda
+    case = C.cfg3(ta, tb)
+    a, b, c = C.cfg_inputs(case, 3, None, normal=True)
+    stream = torch.cuda.Stream()
+    status, out = run_sgemm(torch, handle, case, a, b, c, stream=stream)
+    assert status == 0
+    _assert(check_full(case, a, b, c, out), case.name)
+
+
+@pytest.mark.parametrize("size", [4096, 8192])
+def test_cfg2_large_square(cuda, handle, size):
+    case = C.cfg2(size)
+    a, b, c = C.cfg_inputs(case, 1, 2)
+    status, out = run_sgemm(cuda, handle, case, a, b, c)
+    assert status == 0
+    res = check_sampled(case, a, b, c, out)
+    assert res["all_finite"]
+    _assert(res, case.name)
+
+
+@pytest.mark.parametrize("shape", C.CFG4_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_cfg4_medium_skinny(cuda, handle, shape):
+    case = C.cfg4(*shape)
+    a, b, c = C.cfg_inputs(case, 4, None)
+    status, out = run_sgemm(cuda, handle, case, a, b, c)
+    assert status == 0
+    res = check_sampled(case, a, b, c, out)
+    assert res["all_finite"]
+    _assert(res, case.name)
+
+
+# ---- loader paths, tails, leading dimensions, alignment -----------------------
+PATH_CASES = []
+for ta in (0, 1):
+    for tb in (0, 1):
+        for (m, n, k) in ((300, 200, 70), (257, 129, 33), (1, 1, 1), (5, 300, 17), (511, 3, 1)):
+            for pad, offs in ((0, (0, 0, 0)), (4, (0, 0, 0)), (1, (0, 0, 0)), (0, (1, 2, 3))):
+                PATH_CASES.append((ta, tb, m, n, k, pad, offs))
+
+
+@pytest.mark.parametrize("ta,tb,m,n,k,pad,offs", PATH_CASES)
+def test_paths_tails_alignment(cuda, handle, ta, tb, m, n, k, pad, offs):
+    lda = (k if ta else m) + pad
+    ldb = (n if tb else k) + pad
+    ldc = m + (pad or 1)
+    for alpha, beta in ((1.0, 0.0), (-0.5, 1.0), (0.75, -1.25)):
+        case = C.Case("path", ta, tb, m, n, k, lda, ldb, ldc, alpha, beta)
+        a, b, c = C.cfg_inputs(case, 100 + m + n + k, None)
+        C.pad_and_poison(c, m, n, ldc, beta, C.PRODUCT_PAD)
+        status, out = run_sgemm(cuda, handle, case, a, b, c, offsets=offs)
+        assert status == 0
+        _assert(check_full(case, a, b, c, out), (ta, tb, m, n, k, pad, offs, alpha, beta))
+
+
+def test_deterministic(cuda, handle):
+    case = C.cfg3(0, 0)
+    a, b, c = C.cfg_inputs(case, 3, None, normal=True)
+    _, out1 = run_sgemm(cuda, handle, case, a, b, c)
+    _, out2 = run_sgemm(cuda, handle, case, a, b, c)
+    assert np.array_equal(out1, out2, equal_nan=True)
+
+
+def test_tf32_mode_rejects_work_on_gpu(cuda, handle):
+    torch = cuda
+    case = C.cfg1()
+    a, b, c = C.cfg_inputs(case, 0, -1)
+    handle.set_math_mode(sg.SGBLAS_MATH_TF32)
+    status, out = run_sgemm(torch, handle, case, a, b, c)
+    assert status == sg.SGBLAS_STATUS_NOT_SUPPORTED
+    assert np.array_equal(out, c)
+    handle.set_math_mode(sg.SGBLAS_MATH_FP32)
+
+
+# ---- parity with the reference library itself ---------------------------------
+def test_parity_with_reference_library(cuda, handle):
+    """Both libraries on identical buffers: each within the bound of the FP64
+    oracle, hence within twice the bound of each other."""
+    import oracle
+    try:
+        ref = oracle.RefLib()
+    except (FileNotFoundError, OSError) as e:
+        pytest.skip(f"reference library unavailable: {e}")
+    torch = cuda
+    shapes = [C.cfg3(0, 0), C.cfg3(0, 1), C.cfg3(1, 0), C.cfg3(1, 1),
+              C.Case("768x768x128", 0, 0, 768, 768, 128, 768, 128, 768, -0.375, 0.625),
+              C.Case("1024x2048x64", 0, 0, 1024, 2048, 64, 1024, 64, 1024, 0.625, -0.375)]
+    for case in shapes:
+        a, b, c = C.cfg_inputs(case, 3, None, normal=True)
+        da, pa = to_device(torch, a)
+        db, pb = to_device(torch, b)
+        dc_ref, pc_ref = to_device(torch, c)
+        assert ref.sgemm(case.transa, case.transb, case.m, case.n, case.k, case.alpha, pa,
+                         case.lda, pb, case.ldb, case.beta, pc_ref, case.ldc) == 0
+        torch.cuda.synchronize()
+        out_ref = dc_ref.cpu().numpy()
+        status, out = run_sgemm(torch, handle, case, a, b, c)
+        assert status == 0
+        r_ref = check_full(case, a, b, c, out_ref)
+        r_us = check_full(case, a, b, c, out)
+        assert r_ref["ok_north_star"], ("reference outside the bound?", case.name, r_ref)
+        _assert(r_us, case.name)
+    ref.close()
