@@ -1,0 +1,527 @@
+#!/usr/bin/env python
+"""Headline benchmark: strict-FP32 SGEMM TFLOP/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N == 1: one step = one sgblasSgemm of BASELINE configs[1], 4096^3 NN
+(column-major, lda=ldb=ldc=4096, alpha=1, beta=0), inputs resident in HBM.
+The 256 MiB L2 flush before each step is outside the step's CUDA events.
+
+N > 1 (torchrun, one rank per GPU): one step = one sgblasMgSgemm of BASELINE
+configs[4], 32768 x 32768 x 8192 NN split into N column blocks, A broadcast
+from rank 0 by NCCL inside the step; inputs are > L2 on every rank. value =
+whole-job FLOPs / max over ranks of the timed region (strong scaling).
+
+Printed keys beyond the base contract: e2e (the same metric through the C ABI
+with pinned host inputs copied in and C copied out every step, copies
+pipelined against compute), roofline (FP32 FMA pipe peak = SMs x 128 lanes x
+2 x SM clock sampled during the run), cpu_baseline (the reference's only CPU
+SGEMM arithmetic -- the FP64 oracle loop of tests/cuda/correctness.cu -- on a
+column sample, all host threads), cublas_pedantic (cublasGemmEx with
+CUBLAS_COMPUTE_32F_PEDANTIC on the same buffers), clocks, gpu_launches.
+
+--impl reference: the reference's CPU path on the host cores (the reference
+has no CPU SGEMM; its oracle loop restated in oracle/ is used, "kind": "port").
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import pathlib
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+os.environ.setdefault("NVIDIA_TF32_OVERRIDE", "0")
+
+ROOT = pathlib.Path(__file__).resolve().parent
+METRIC = "strict-FP32 SGEMM TFLOP/s at 4096³ NN vs cuBLAS pedantic and FP32 FMA peak"
+UNIT = "TFLOP/s"
+FP32_LANES_PER_SM = 128
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--size", type=int, default=4096, help="N=1 square size (4096 headline)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during a region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        # median of the busy samples (the region is bracketed by idle time)
+        busy = [s for s in sm if s >= 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def smi_index(torch, dev: int) -> str:
+    props = torch.cuda.get_device_properties(dev)
+    bus = getattr(props, "pci_bus_id", None)
+    dom = getattr(props, "pci_domain_id", None)
+    did = getattr(props, "pci_device_id", None)
+    if bus is not None and dom is not None and did is not None:
+        return f"{dom:08x}:{bus:02x}:{did:02x}.0"
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        return vis.split(",")[dev]
+    return str(dev)
+
+
+# ---------------------------------------------------------------------------
+class Cublas:
+    """cublasGemmEx with CUBLAS_COMPUTE_32F_PEDANTIC (comparison lane only)."""
+
+    def __init__(self):
+        self.lib = None
+        for name in ("libcublas.so.12", "libcublas.so"):
+            try:
+                self.lib = ctypes.CDLL(name)
+                break
+            except OSError:
+                continue
+        if self.lib is None:
+            raise OSError("libcublas not found")
+        self.h = ctypes.c_void_p()
+        assert self.lib.cublasCreate_v2(ctypes.byref(self.h)) == 0
+        assert self.lib.cublasSetMathMode(self.h, 2) == 0   # CUBLAS_PEDANTIC_MATH
+        ver = ctypes.c_int()
+        self.lib.cublasGetVersion_v2(self.h, ctypes.byref(ver))
+        self.version = ver.value
+        f = self.lib.cublasGemmEx
+        vp, ip = ctypes.c_void_p, ctypes.c_int
+        f.argtypes = [vp, ip, ip, ip, ip, ip, vp, vp, ip, ip, vp, ip, ip, vp, vp, ip, ip, ip, ip]
+
+    def set_stream(self, stream) -> None:
+        self.lib.cublasSetStream_v2(self.h, ctypes.c_void_p(stream.cuda_stream))
+
+    def sgemm(self, ta, tb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc) -> int:
+        al = ctypes.c_float(alpha)
+        be = ctypes.c_float(beta)
+        return self.lib.cublasGemmEx(self.h, ta, tb, m, n, k, ctypes.byref(al), a, 0, lda, b, 0,
+                                     ldb, ctypes.byref(be), c, 0, ldc, 69, -1)
+
+
+def profile_traffic(name: str):
+    """DRAM bytes per launch recorded from an ncu capture (profiles/<name>)."""
+    path = ROOT / "profiles" / name
+    if not path.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch\s*[:=]\s*([0-9.eE+]+)", path.read_text())
+    return float(m.group(1)) if m else None
+
+
+def fp32_peak_tflops(sms: int, mhz: float) -> float:
+    return sms * FP32_LANES_PER_SM * 2 * mhz * 1e6 / 1e12
+
+
+# ---------------------------------------------------------------------------
+def cpu_baseline(a, b, m, n, k, lda, ldb, budget_s: float) -> dict:
+    """The oracle loop (FP32 in, FP64 accumulate) on a column sample of the
+    workload, all host threads; rate extrapolated per column."""
+    import numpy as np
+
+    import oracle
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    c = np.zeros(m * threads, dtype=np.float32)
+    t0 = time.perf_counter()
+    oracle.sgemm_cpu(0, 0, m, k, 1.0, a, lda, b, ldb, 0.0, c, m, 0, threads, threads)
+    t_one = time.perf_counter() - t0
+    rounds = max(1, min(int(budget_s / max(t_one, 1e-3)), n // threads))
+    cols = rounds * threads
+    c = np.zeros(m * cols, dtype=np.float32)
+    t0 = time.perf_counter()
+    oracle.sgemm_cpu(0, 0, m, k, 1.0, a, lda, b, ldb, 0.0, c, m, 0, cols, threads)
+    dt = time.perf_counter() - t0
+    rate = 2.0 * m * k * cols / dt / 1e12
+    return {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"columns 0..{cols - 1} of C ({cols}/{n}) of the {m}x{n}x{k} NN workload, "
+                      f"FP64-accumulated oracle loop of tests/cuda/correctness.cu:373-392, "
+                      f"{dt:.1f} s, rate extrapolated per column",
+            "seconds": dt}
+
+
+# ---------------------------------------------------------------------------
+def run_reference(args) -> None:
+    """--impl reference: the reference's CPU path (oracle port) on host cores."""
+    import numpy as np
+
+    import oracle
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps = args.steps if args.steps is not None else 5
+    warmup = args.warmup if args.warmup is not None else 1
+    m = n = k = args.size
+    rng = np.random.default_rng(1)
+    a = rng.uniform(-1.0, 1.0, m * k).astype(np.float32)
+    b = rng.uniform(-1.0, 1.0, k * n).astype(np.float32)
+    threads = len(os.sched_getaffinity(0))
+    cols = threads          # one column per thread per step (a bounded sample)
+    c = np.zeros(m * cols, dtype=np.float32)
+    for _ in range(warmup):
+        oracle.sgemm_cpu(0, 0, m, k, 1.0, a, m, b, k, 0.0, c, m, 0, cols, threads)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        oracle.sgemm_cpu(0, 0, m, k, 1.0, a, m, b, k, 0.0, c, m, 0, cols, threads)
+        times.append(time.perf_counter() - t0)
+    rate = 2.0 * m * k * cols * steps / sum(times) / 1e12
+    sample = (f"{cols} columns of C per step of the {m}^3 NN workload ({threads} threads, one "
+              f"column each), FP64-accumulated oracle loop of tests/cuda/correctness.cu:373-392")
+    out = {"metric": METRIC, "value": rate, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+           "steps": steps, "warmup": warmup, "ms_per_step": 1e3 * sum(times) / steps,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic",
+           "config": {"workload": f"sgemm NN {m}x{n}x{k} column-major alpha=1 beta=0 "
+                                  "(BASELINE configs[1]); per step a column sample"},
+           "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "note": "the reference has no CPU SGEMM (src/sgemm_host.cpp:26-27 returns "
+                   "NOT_SUPPORTED); its only CPU GEMM arithmetic is the FP64 oracle loop"}
+    print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def run_single(args) -> None:
+    import numpy as np
+    import torch
+
+    import sgblas_b200 as sg
+
+    steps = args.steps if args.steps is not None else 200
+    warmup = max(3, args.warmup if args.warmup is not None else 20)
+    dev = 0
+    torch.cuda.set_device(dev)
+    props = torch.cuda.get_device_properties(dev)
+    sms = props.multi_processor_count
+    m = n = k = args.size
+    lda = ldb = ldc = m
+    flops = 2.0 * m * n * k
+
+    rng = np.random.default_rng(1)
+    ha = rng.uniform(-1.0, 1.0, m * k).astype(np.float32)
+    hb = rng.uniform(-1.0, 1.0, k * n).astype(np.float32)
+    hc = np.random.default_rng(2).uniform(-1.0, 1.0, m * n).astype(np.float32)
+    da = torch.from_numpy(ha).cuda()
+    db = torch.from_numpy(hb).cuda()
+    dc = torch.from_numpy(hc).cuda()
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    stream = torch.cuda.Stream()
+    h = sg.Handle()
+    h.set_stream(stream)
+
+    def launch():
+        h.sgemm(0, 0, m, n, k, 1.0, da, lda, db, ldb, 0.0, dc, ldc)
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            flush.zero_()
+            launch()
+    torch.cuda.synchronize()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    with ClockSampler(smi_index(torch, dev)) as clk:
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for i in range(steps):
+                flush.zero_()
+                ev[i][0].record(stream)
+                launch()
+                ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    times_ms = [s.elapsed_time(e) for s, e in ev]
+    total_s = sum(times_ms) / 1e3
+    value = flops * steps / total_s / 1e12
+    clocks = clk.summary()
+    if sg.get_device_errors() != 0:
+        raise RuntimeError("device error flags raised during the bench")
+
+    mhz = clocks["sm_mhz"] or 1965.0
+    peak = fp32_peak_tflops(sms, mhz)
+    traffic = profile_traffic(f"sgemm_nn_{m}.md")
+    roofline = {"bound": "fp32_fma", "achieved": value, "peak": peak, "unit": UNIT,
+                "frac": value / peak, "traffic": traffic,
+                "peak_source": f"{sms} SMs x {FP32_LANES_PER_SM} FP32 lanes x 2 x {mhz:.0f} MHz "
+                               "(median SM clock sampled during the timed region); "
+                               "MEASURED_PEAKS.json has no FP32 CUDA-core figure",
+                "frac_of_max_clock": value / fp32_peak_tflops(sms, 1965.0),
+                "algorithmic_flops_per_launch": flops,
+                "algorithmic_bytes_per_launch": 4.0 * (m * k + k * n + m * n)}
+
+    out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": steps,
+           "warmup": warmup, "ms_per_step": 1e3 * total_s / steps, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None,
+           "vs_published_a100": value / 17.736,
+           "dtype": "f32", "data": "synthetic",
+           "config": {"workload": f"sgemm NN {m}x{n}x{k} column-major alpha=1 beta=0 "
+                                  "(BASELINE configs[1])",
+                      "m": m, "n": n, "k": k, "lda": lda, "ldb": ldb, "ldc": ldc,
+                      "inputs": "uniform[-1,1) float32 (numpy seeds 1: A,B; 2: C)",
+                      "l2": "flushed before every timed step (256 MiB write outside the "
+                            "step's CUDA events)"},
+           "roofline": roofline, "clocks": clocks, "gpu_launches": steps,
+           "device": props.name}
+
+    if not args.no_cublas:
+        try:
+            cb = Cublas()
+            cb.set_stream(stream)
+            dc2 = torch.empty_like(dc)
+            for _ in range(warmup):
+                cb.sgemm(0, 0, m, n, k, 1.0, da.data_ptr(), lda, db.data_ptr(), ldb, 0.0,
+                         dc2.data_ptr(), ldc)
+            cev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(steps)]
+            with torch.cuda.stream(stream):
+                for i in range(steps):
+                    flush.zero_()
+                    cev[i][0].record(stream)
+                    st = cb.sgemm(0, 0, m, n, k, 1.0, da.data_ptr(), lda, db.data_ptr(), ldb,
+                                  0.0, dc2.data_ptr(), ldc)
+                    cev[i][1].record(stream)
+            torch.cuda.synchronize()
+            assert st == 0
+            cval = flops * steps / (sum(s.elapsed_time(e) for s, e in cev) / 1e3) / 1e12
+            out["cublas_pedantic"] = {"value": cval, "unit": UNIT, "ratio": value / cval,
+                                      "version": cb.version,
+                                      "call": "cublasGemmEx CUDA_R_32F x3, "
+                                              "CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_PEDANTIC_MATH, "
+                                              "NVIDIA_TF32_OVERRIDE=0"}
+            del dc2
+        except (OSError, AssertionError) as e:
+            out["cublas_pedantic"] = {"unavailable": str(e)}
+
+    if not args.no_e2e:
+        out["e2e"] = e2e_single(torch, sg, ha, hb, m, n, k, max(10, steps // 4), warmup)
+    if not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(ha, hb, m, n, k, lda, ldb, args.cpu_seconds)
+    h.close()
+    print(json.dumps(out), flush=True)
+
+
+def e2e_single(torch, sg, ha, hb, m, n, k, steps, warmup) -> dict:
+    """The metric through the public C ABI with host buffers: each step copies
+    A and B from pinned host memory, runs sgblasSgemm and copies C back.
+    Two device buffer sets; copies of step i+1 overlap the SGEMM of step i."""
+    pa = torch.from_numpy(ha).pin_memory()
+    pb = torch.from_numpy(hb).pin_memory()
+    pc = torch.empty(m * n, dtype=torch.float32).pin_memory()
+    sets = [(torch.empty(m * k, device="cuda"), torch.empty(k * n, device="cuda"),
+             torch.empty(m * n, device="cuda")) for _ in range(2)]
+    s_in, s_comp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    h = sg.Handle()
+    h.set_stream(s_comp)
+    in_done = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+
+    def run(count):
+        for i in range(count):
+            j = i % 2
+            da, db, dc = sets[j]
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(comp_done[j])     # set j free for new inputs
+                da.copy_(pa, non_blocking=True)
+                db.copy_(pb, non_blocking=True)
+                in_done[j].record(s_in)
+            s_comp.wait_event(in_done[j])
+            if i >= 2:
+                s_comp.wait_event(out_done[j])        # C of step i-2 has left
+            h.sgemm(0, 0, m, n, k, 1.0, da, m, db, k, 0.0, dc, m)
+            comp_done[j].record(s_comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(comp_done[j])
+                pc.copy_(dc, non_blocking=True)
+                out_done[j].record(s_out)
+
+    run(warmup)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s_in)
+    run(steps)
+    s_in.wait_stream(s_out)
+    end.record(s_in)
+    torch.cuda.synchronize()
+    secs = start.elapsed_time(end) / 1e3
+    h.close()
+    return {"value": 2.0 * m * n * k * steps / secs / 1e12, "unit": UNIT,
+            "h2d_bytes_per_step": 4 * (m * k + k * n), "d2h_bytes_per_step": 4 * m * n,
+            "steps": steps, "pipelining": "2 buffer sets; H2D, SGEMM and D2H on 3 streams"}
+
+
+# ---------------------------------------------------------------------------
+def run_sharded(args) -> None:
+    """N ranks: config 5, 32768 x 32768 x 8192 NN, columns split across ranks,
+    A broadcast from rank 0 inside every step (sgblasMgSgemm)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import sgblas_b200 as sg
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    steps = args.steps if args.steps is not None else 5
+    warmup = max(3, args.warmup if args.warmup is not None else 3)
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    M, N, K = 32768, 32768, 8192
+    assert N % world == 0
+    n_loc = N // world
+    flops = 2.0 * M * N * K
+
+    uid = [sg.mg_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    mg = sg.MgHandle(world, rank, uid[0], local)
+    stream = torch.cuda.Stream()
+    mg.set_stream(stream)
+
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5 + rank)
+    a = torch.empty(M * K, device="cuda")
+    if rank == 0:
+        a.uniform_(-1.0, 1.0, generator=gen)
+    b = torch.empty(K * n_loc, device="cuda").uniform_(-1.0, 1.0, generator=gen)
+    c = torch.empty(M * n_loc, device="cuda")
+
+    def step():
+        mg.sgemm(0, 0, M, n_loc, K, 1.0, a, M, 0, b, K, 0.0, c, M)
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    with ClockSampler(smi_index(torch, local)) as clk:
+        torch.cuda.synchronize()
+        dist.barrier()
+        with torch.cuda.stream(stream):
+            for i in range(steps):
+                ev[i][0].record(stream)
+                step()
+                ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+    local_s = sum(s.elapsed_time(e) for s, e in ev) / 1e3
+    t = torch.tensor([local_s], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_s = float(t.item())
+    value = flops * steps / total_s / 1e12
+    clocks = clk.summary()
+    allc = [None] * world
+    dist.all_gather_object(allc, clocks)
+    mg.close()
+    props = torch.cuda.get_device_properties(local)
+    sms = props.multi_processor_count
+    mhz = statistics.median([x["sm_mhz"] for x in allc if x["sm_mhz"]] or [1965.0])
+    peak = world * fp32_peak_tflops(sms, mhz)
+    if rank == 0:
+        reasons = sorted({r for x in allc for r in x["reasons"]})
+        out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+               "warmup": warmup, "ms_per_step": 1e3 * total_s / steps, "higher_is_better": True,
+               "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+               "config": {"workload": f"sharded sgemm NN {M}x{N}x{K} (BASELINE configs[4]), "
+                                      f"B and C split into {world} column blocks of {n_loc}, "
+                                      "A (1 GiB) broadcast from rank 0 by NCCL in every step",
+                          "parallelism": f"column-shard x{world}", "l2": "inputs larger than L2"},
+               "roofline": {"bound": "fp32_fma", "achieved": value, "peak": peak, "unit": UNIT,
+                            "frac": value / peak, "traffic": None,
+                            "peak_source": f"{world} x {sms} SMs x 128 lanes x 2 x {mhz:.0f} MHz"},
+               "clocks": {"sm_mhz": mhz, "sm_max_mhz": max((x["sm_max_mhz"] or 0) for x in allc),
+                          "reasons": reasons},
+               "gpu_launches": steps}
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    sys.path.insert(0, str(ROOT))
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 or args.gpus > 1:
+        if world == 1:
+            raise SystemExit("--gpus > 1 must be launched with torchrun (one rank per GPU)")
+        run_sharded(args)
+    else:
+        run_single(args)
+
+
+if __name__ == "__main__":
+    main()

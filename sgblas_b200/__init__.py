@@ -8,7 +8,7 @@ entry-point names, the same argument meaning and the same status codes
 of AG0708/sgBLAS), plus a small object wrapper (:class:`Handle`).
 
 There is no CPU fallback: importing this module fails loudly when the library
-has not been built (``python -m sgblas_b200.build``).
+has not been built (``python sgblas_b200/build.py``).
 """
 from __future__ import annotations
 
@@ -21,7 +21,7 @@ __all__ = [
     "SGBLAS_STATUS_INVALID_VALUE", "SGBLAS_STATUS_ARCH_MISMATCH",
     "SGBLAS_STATUS_EXECUTION_FAILED", "SGBLAS_STATUS_INTERNAL_ERROR",
     "SGBLAS_STATUS_NOT_SUPPORTED", "SGBLAS_OP_N", "SGBLAS_OP_T", "SGBLAS_MATH_FP32",
-    "SGBLAS_MATH_TF32", "EXPORTED_SYMBOLS",
+    "SGBLAS_MATH_TF32", "EXPORTED_SYMBOLS", "MgHandle", "mg_unique_id", "get_device_errors",
 ]
 
 LIB_PATH = pathlib.Path(__file__).resolve().parent / "lib" / "libsgblas.so"
@@ -57,6 +57,19 @@ _SIGNATURES = {
                                     ctypes.c_void_p, ctypes.c_int]),
     "sgblasGetStatusString": (ctypes.c_char_p, [ctypes.c_int]),
     "sgblasGetDeviceErrors": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]),
+    # multi-GPU extension (include/sgblas/sgblas_mg.h)
+    "sgblasMgGetUniqueId": (ctypes.c_int, [ctypes.c_void_p]),
+    "sgblasMgCreate": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_void_p, ctypes.c_int]),
+    "sgblasMgDestroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "sgblasMgSetStream": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "sgblasMgGetRank": (ctypes.c_int, [ctypes.c_void_p, _c_int_p, _c_int_p]),
+    "sgblasMgSgemm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int, ctypes.c_int, _c_float_p, ctypes.c_void_p,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                      _c_float_p, ctypes.c_void_p, ctypes.c_int]),
+    "sgblasMgAllGather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_size_t]),
 }
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)
 
@@ -64,7 +77,7 @@ EXPORTED_SYMBOLS = tuple(_SIGNATURES)
 def _load() -> ctypes.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(
-            f"{LIB_PATH} is missing: build it with `python -m sgblas_b200.build` "
+            f"{LIB_PATH} is missing: build it with `python sgblas_b200/build.py` "
             "(there is no CPU fallback)")
     dll = ctypes.CDLL(str(LIB_PATH))
     for name, (res, args) in _SIGNATURES.items():
@@ -162,6 +175,46 @@ class Handle:
     def sgemm(self, transa, transb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc) -> None:
         _check("sgblasSgemm",
                self.sgemm_status(transa, transb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc))
+
+
+MG_UNIQUE_ID_BYTES = 128
+
+
+def mg_unique_id() -> bytes:
+    """A fresh NCCL unique id (call on one rank, share the bytes)."""
+    buf = (ctypes.c_ubyte * MG_UNIQUE_ID_BYTES)()
+    _check("sgblasMgGetUniqueId", lib.sgblasMgGetUniqueId(buf))
+    return bytes(buf)
+
+
+class MgHandle:
+    """One rank of a column-sharded multi-GPU SGEMM (sgblas_mg.h)."""
+
+    def __init__(self, nranks: int, rank: int, unique_id: bytes, device: int):
+        raw = ctypes.c_void_p()
+        uid = (ctypes.c_ubyte * MG_UNIQUE_ID_BYTES).from_buffer_copy(unique_id)
+        _check("sgblasMgCreate", lib.sgblasMgCreate(ctypes.byref(raw), nranks, rank, uid, device))
+        self._h = raw
+
+    def close(self) -> None:
+        if self._h is not None and self._h.value is not None:
+            _check("sgblasMgDestroy", lib.sgblasMgDestroy(self._h))
+        self._h = None
+
+    def set_stream(self, stream) -> None:
+        _check("sgblasMgSetStream",
+               lib.sgblasMgSetStream(self._h, getattr(stream, "cuda_stream", stream)))
+
+    def sgemm_status(self, transa, transb, m, n_local, k, alpha, a, lda, root, b, ldb, beta, c,
+                     ldc) -> int:
+        return lib.sgblasMgSgemm(self._h, transa, transb, m, n_local, k, _fp(alpha), _ptr(a), lda,
+                                 root, _ptr(b), ldb, _fp(beta), _ptr(c), ldc)
+
+    def sgemm(self, *args) -> None:
+        _check("sgblasMgSgemm", self.sgemm_status(*args))
+
+    def all_gather(self, send, recv, count: int) -> None:
+        _check("sgblasMgAllGather", lib.sgblasMgAllGather(self._h, _ptr(send), _ptr(recv), count))
 
 
 def get_device_errors(clear: bool = True) -> int:

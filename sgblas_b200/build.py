@@ -1,6 +1,7 @@
 """Builds libsgblas.so (the product) in-tree with nvcc for sm_100a.
 
-    python -m sgblas_b200.build          # or: from sgblas_b200.build import build
+    python sgblas_b200/build.py [-v]     (a script: it must not import the package,
+                                          whose import loads the library it builds)
 
 Every translation unit under sgblas_b200/csrc is compiled for
 ``-gencode arch=compute_100a,code=sm_100a`` with ``-lineinfo`` and linked into

@@ -16,10 +16,14 @@ struct sgblasContext {
   sgblasStream_t stream = nullptr;
   sgblasMathMode_t math_mode = SGBLAS_MATH_FP32;
 
-  // Split-K partial sums (FP32). device == -1 means nothing allocated.
+  // Stream-K workspace: arrival counters, then FP32 partial-tile slots.
+  // device == -1 means nothing allocated. `workspace_event` (a cudaEvent_t)
+  // marks the last launch that used the workspace, so that a launch on a
+  // different stream is ordered after it.
   void *workspace = nullptr;
   std::size_t workspace_bytes = 0;
   int workspace_device = -1;
+  void *workspace_event = nullptr;
 };
 
 namespace sgblas::detail {

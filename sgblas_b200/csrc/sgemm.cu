@@ -15,6 +15,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cstdint>
 
@@ -104,10 +106,107 @@ bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// ---------------------------------------------------------------------------
+// Persistent schedule: one CTA per SM. Whole tiles are dealt round-robin;
+// when the tile count leaves a partial last wave, the last (full wave +
+// remainder) tiles are split by k iterations over all CTAs (stream-K), so every
+// SM finishes at the same time. Small problems with fewer tiles than SMs are
+// split the same way, down to kMinSkIters k slices per CTA.
+struct Schedule {
+  int grid = 0, dp_tiles = 0, sk_tiles = 0, sk_q = 0, sk_r = 0;
+};
+
+constexpr int kMinSkIters = 8;
+
+Schedule makeSchedule(long long tiles, int kiters, int sms) {
+  Schedule s;
+  const int t = static_cast<int>(tiles);
+  if (t >= sms) {
+    s.grid = sms;
+    const int waves = t / sms, rem = t % sms;
+    if (rem == 0 || kiters < 2 * kMinSkIters) {
+      s.dp_tiles = t;
+    } else {
+      s.dp_tiles = (waves - 1) * sms;
+      s.sk_tiles = t - s.dp_tiles;
+    }
+  } else {
+    const long long iters = tiles * kiters;
+    s.grid = static_cast<int>(
+        std::min<long long>(sms, std::max<long long>(tiles, iters / kMinSkIters)));
+    if (s.grid == t) s.dp_tiles = t;
+    else s.sk_tiles = t;
+  }
+  if (s.sk_tiles > 0) {
+    const long long it = static_cast<long long>(s.sk_tiles) * kiters;
+    s.sk_q = static_cast<int>(it / s.grid);
+    s.sk_r = static_cast<int>(it % s.grid);
+  }
+  return s;
+}
+
+int smCount(int device) {
+  static std::atomic<int> cached[kMaxDevices];
+  if (device < 0 || device >= kMaxDevices) return 0;
+  int v = cached[device].load(std::memory_order_relaxed);
+  if (v == 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return 0;
+    }
+    cached[device].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+constexpr size_t kSlotBytes = size_t{kern::kThreads} * 32 * sizeof(float4);
+
+// Grow-only, stream-ordered workspace of the handle: [counters | slots].
+// Returns false (and the caller falls back to whole-tile scheduling) when it
+// cannot be provided.
+bool ensureWorkspace(sgblasContext *ctx, size_t counter_bytes, size_t slot_bytes, int device,
+                     cudaStream_t stream) {
+  const size_t need = counter_bytes + slot_bytes;
+  if (ctx->workspace != nullptr && ctx->workspace_device == device &&
+      ctx->workspace_bytes >= need) {
+    if (ctx->workspace_event != nullptr &&
+        cudaStreamWaitEvent(stream, static_cast<cudaEvent_t>(ctx->workspace_event), 0) !=
+            cudaSuccess) {
+      (void)cudaGetLastError();
+      return false;
+    }
+    return true;
+  }
+  releaseWorkspace(ctx);
+  if (cudaSetDevice(device) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  const size_t bytes = std::max(need, size_t{64} << 20);  // room for later, larger calls
+  void *ws = nullptr;
+  cudaEvent_t ev = nullptr;
+  if (cudaMallocAsync(&ws, bytes, stream) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  // Counters must start at zero; every launch leaves them at zero again.
+  if (cudaMemsetAsync(ws, 0, bytes, stream) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+    (void)cudaGetLastError();
+    (void)cudaFreeAsync(ws, stream);
+    return false;
+  }
+  ctx->workspace = ws;
+  ctx->workspace_bytes = bytes;
+  ctx->workspace_device = device;
+  ctx->workspace_event = ev;
+  return true;
+}
+
 template <bool kTA, bool kTB, Beta kBeta, Src kSrc>
-sgblasStatus_t launchTiles(GemmParams p, int device, cudaStream_t stream) {
+sgblasStatus_t launchTiles(GemmParams p, sgblasContext *ctx, int device, cudaStream_t stream) {
   using Plan = kern::Plan<kTA, kTB, kSrc>;
-  auto kernel = kern::sgemmTileKernel<kTA, kTB, kBeta, kSrc>;
+  auto kernel = kern::sgemmKernel<kTA, kTB, kBeta, kSrc>;
   static std::atomic<uint64_t> configured{0};
   if (!configureKernel(reinterpret_cast<const void *>(kernel), device, kern::kSmemBytes,
                        &configured))
@@ -115,21 +214,50 @@ sgblasStatus_t launchTiles(GemmParams p, int device, cudaStream_t stream) {
   p.tiles_m = (p.m + Plan::kBM - 1) / Plan::kBM;
   p.tiles_n = (p.n + Plan::kBN - 1) / Plan::kBN;
   p.group_m = 8;
+  p.kiters = (p.k + kern::kBK - 1) / kern::kBK;
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
-  if (tiles > INT_MAX) return SGBLAS_STATUS_NOT_SUPPORTED;
+  if (tiles > INT_MAX / 2 || static_cast<long long>(p.kiters) * tiles > INT_MAX)
+    return SGBLAS_STATUS_NOT_SUPPORTED;
+  const int sms = smCount(device);
+  if (sms <= 0) return SGBLAS_STATUS_EXECUTION_FAILED;
+  Schedule s = makeSchedule(tiles, p.kiters, sms);
+  if (s.sk_tiles > 0) {
+    const size_t counter_bytes = (static_cast<size_t>(s.sk_tiles) * sizeof(int) + 255) & ~size_t{255};
+    if (ensureWorkspace(ctx, counter_bytes, 2 * static_cast<size_t>(s.grid) * kSlotBytes, device,
+                        stream)) {
+      p.counters = static_cast<int *>(ctx->workspace);
+      p.ws = reinterpret_cast<float4 *>(static_cast<char *>(ctx->workspace) + counter_bytes);
+    } else {  // no workspace: whole tiles only
+      s = Schedule{};
+      s.grid = static_cast<int>(std::min<long long>(tiles, sms));
+      s.dp_tiles = static_cast<int>(tiles);
+    }
+  }
+  p.grid = s.grid;
+  p.dp_tiles = s.dp_tiles;
+  p.sk_tiles = s.sk_tiles;
+  p.sk_q = s.sk_q;
+  p.sk_r = s.sk_r;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(tiles));
+  cfg.gridDim = dim3(static_cast<unsigned>(s.grid));
   cfg.blockDim = dim3(kern::kThreads);
   cfg.dynamicSmemBytes = kern::kSmemBytes;
   cfg.stream = stream;
-  return launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));
+  const sgblasStatus_t st = launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));
+  if (st == SGBLAS_STATUS_SUCCESS && s.sk_tiles > 0 &&
+      cudaEventRecord(static_cast<cudaEvent_t>(ctx->workspace_event), stream) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  }
+  return st;
 }
 
 template <bool kTA, bool kTB, Src kSrc>
-sgblasStatus_t launchByBeta(const GemmParams &p, int device, cudaStream_t stream) {
-  if (p.beta == 0.0F) return launchTiles<kTA, kTB, Beta::kZero, kSrc>(p, device, stream);
-  if (p.beta == 1.0F) return launchTiles<kTA, kTB, Beta::kOne, kSrc>(p, device, stream);
-  return launchTiles<kTA, kTB, Beta::kGeneral, kSrc>(p, device, stream);
+sgblasStatus_t launchByBeta(const GemmParams &p, sgblasContext *ctx, int device,
+                            cudaStream_t stream) {
+  if (p.beta == 0.0F) return launchTiles<kTA, kTB, Beta::kZero, kSrc>(p, ctx, device, stream);
+  if (p.beta == 1.0F) return launchTiles<kTA, kTB, Beta::kOne, kSrc>(p, ctx, device, stream);
+  return launchTiles<kTA, kTB, Beta::kGeneral, kSrc>(p, ctx, device, stream);
 }
 
 // TMA descriptors for the operand tiles the kernel stages: a [k][x] tile is a
@@ -151,21 +279,22 @@ bool encodeOperands(GemmParams &p) {
 }
 
 template <bool kTA, bool kTB>
-sgblasStatus_t launchBySource(GemmParams &p, int device, cudaStream_t stream) {
+sgblasStatus_t launchBySource(GemmParams &p, sgblasContext *ctx, int device, cudaStream_t stream) {
   // TMA needs 16-byte aligned bases and leading dimensions that are a
   // multiple of 16 bytes; TN has no [k][x] operand for TMA to deliver.
   if constexpr (!(kTA && !kTB)) {
     if (aligned16(p.a) && aligned16(p.b) && p.lda % 4 == 0 && p.ldb % 4 == 0 &&
         encodeOperands<kTA, kTB>(p)) {
-      return launchByBeta<kTA, kTB, Src::kTma>(p, device, stream);
+      return launchByBeta<kTA, kTB, Src::kTma>(p, ctx, device, stream);
     }
   }
-  return launchByBeta<kTA, kTB, Src::kCopy>(p, device, stream);
+  return launchByBeta<kTA, kTB, Src::kCopy>(p, ctx, device, stream);
 }
 
-sgblasStatus_t launchProduct(sgblasOperation_t ta, sgblasOperation_t tb, int m, int n, int k,
-                             float alpha, const float *a, int lda, const float *b, int ldb,
-                             float beta, float *c, int ldc, cudaStream_t stream) {
+sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOperation_t tb,
+                             int m, int n, int k, float alpha, const float *a, int lda,
+                             const float *b, int ldb, float beta, float *c, int ldc,
+                             cudaStream_t stream) {
   int device = -1;
   if (cudaGetDevice(&device) != cudaSuccess) {
     (void)cudaGetLastError();
@@ -189,10 +318,10 @@ sgblasStatus_t launchProduct(sgblasOperation_t ta, sgblasOperation_t tb, int m, 
   p.err = err;
 
   const bool tA = ta == SGBLAS_OP_T, tB = tb == SGBLAS_OP_T;
-  if (!tA && !tB) return launchBySource<false, false>(p, device, stream);
-  if (!tA && tB) return launchBySource<false, true>(p, device, stream);
-  if (tA && !tB) return launchBySource<true, false>(p, device, stream);
-  return launchBySource<true, true>(p, device, stream);
+  if (!tA && !tB) return launchBySource<false, false>(p, ctx, device, stream);
+  if (!tA && tB) return launchBySource<false, true>(p, ctx, device, stream);
+  if (tA && !tB) return launchBySource<true, false>(p, ctx, device, stream);
+  return launchBySource<true, true>(p, ctx, device, stream);
 }
 
 }  // namespace
@@ -202,8 +331,11 @@ void releaseWorkspace(sgblasContext *context) {
     int current = -1;
     const bool restore = cudaGetDevice(&current) == cudaSuccess;
     if (cudaSetDevice(context->workspace_device) == cudaSuccess) {
-      (void)cudaFree(context->workspace);
+      (void)cudaFree(context->workspace);  // synchronizes with the launches using it
+      if (context->workspace_event != nullptr)
+        (void)cudaEventDestroy(static_cast<cudaEvent_t>(context->workspace_event));
     }
+    context->workspace_event = nullptr;
     if (restore) (void)cudaSetDevice(current);
     (void)cudaGetLastError();
     context->workspace = nullptr;
@@ -228,6 +360,6 @@ extern "C" sgblasStatus_t sgblasSgemm(sgblasHandle_t handle, sgblasOperation_t t
   if (handle->math_mode != SGBLAS_MATH_FP32) return SGBLAS_STATUS_NOT_SUPPORTED;
   const auto stream = static_cast<cudaStream_t>(handle->stream);
   if (plan.work == Work::kScale) return launchScale(m, n, plan.beta, c, ldc, stream);
-  return launchProduct(transa, transb, m, n, k, plan.alpha, a, lda, b, ldb, plan.beta, c, ldc,
-                       stream);
+  return launchProduct(handle, transa, transb, m, n, k, plan.alpha, a, lda, b, ldb, plan.beta, c,
+                       ldc, stream);
 }

@@ -73,7 +73,66 @@ struct GemmParams {
   int tiles_m, tiles_n;
   int group_m;        // raster: tile rows per CTA group
   unsigned *err;      // device error word
+  // Persistent schedule (see the kernel comment): tiles [0, dp_tiles) are
+  // whole-tile work dealt round-robin to the CTAs; tiles [dp_tiles,
+  // dp_tiles + sk_tiles) are split by k iterations ("stream-K"): CTA c owns
+  // iterations [c*sk_q + min(c, sk_r), (c+1)*sk_q + min(c+1, sk_r)).
+  int kiters;         // k iterations (BK slices) per tile
+  int grid;           // persistent CTAs
+  int dp_tiles;
+  int sk_tiles;
+  int sk_q, sk_r;
+  float4 *ws;         // 2 * grid partial-tile slots of kThreads * 32 float4
+  int *counters;      // sk_tiles arrival counters, zero between launches
 };
+
+// One unit of a CTA's work: k iterations [kb, ke) of tile `tile`.
+struct Item {
+  int tile, kb, ke;
+};
+
+// Producer position: item index, k iteration, item end, tile origin.
+struct Cursor {
+  int idx, kt, ke, m0, n0;
+};
+
+__device__ __forceinline__ int skBegin(const GemmParams &p, int c) {
+  return c * p.sk_q + min(c, p.sk_r);
+}
+
+// The CTA owning stream-K iteration x (inverse of skBegin).
+__device__ __forceinline__ int skOwner(const GemmParams &p, int x) {
+  const int head = p.sk_r * (p.sk_q + 1);
+  return x < head ? x / (p.sk_q + 1) : p.sk_r + (x - head) / p.sk_q;
+}
+
+__device__ __forceinline__ int dpItems(const GemmParams &p, int c) {
+  return c < p.dp_tiles ? (p.dp_tiles - 1 - c) / p.grid + 1 : 0;
+}
+
+__device__ __forceinline__ int numItems(const GemmParams &p, int c) {
+  int n = dpItems(p, c);
+  if (p.sk_tiles > 0) {
+    const int s = skBegin(p, c), e = skBegin(p, c + 1);
+    if (e > s) n += (e - 1) / p.kiters - s / p.kiters + 1;
+  }
+  return n;
+}
+
+__device__ __forceinline__ Item itemAt(const GemmParams &p, int c, int idx) {
+  const int ndp = dpItems(p, c);
+  if (idx < ndp) return {c + idx * p.grid, 0, p.kiters};
+  const int s = skBegin(p, c), e = skBegin(p, c + 1);
+  const int u = s / p.kiters + (idx - ndp);
+  const int base = u * p.kiters;
+  return {p.dp_tiles + u, max(s, base) - base, min(e, base + p.kiters) - base};
+}
+
+// Workspace slot of CTA c's piece of stream-K tile u: slot 2c holds the piece
+// of the first tile c touches, slot 2c+1 the piece of its last one.
+__device__ __forceinline__ int skSlot(const GemmParams &p, int c, int u) {
+  return 2 * c + (u == skBegin(p, c) / p.kiters ? 0 : 1);
+}
 
 // Byte offset of element (x, k) inside a kKX tile.
 __device__ __forceinline__ uint32_t kxOffset(int x, int k) {
@@ -209,11 +268,20 @@ __device__ __forceinline__ float epilogueValue(float acc, float alpha, float bet
   }
 }
 
-// ---- the kernel: one tile of C per CTA --------------------------------------
+// ---- the persistent kernel ----------------------------------------------------
+// Each CTA walks its items in order (whole tiles first, then its stream-K
+// range). The k iterations of consecutive items form one flat stream, so the
+// stage ring keeps prefetching the next tile while the current one finishes.
+// A stream-K piece that does not cover its whole tile is published to the
+// workspace; the CTA that publishes the last piece of a tile (an atomic
+// arrival count, no waiting) sums every piece in piece order -- the order is
+// fixed by the schedule, so results do not depend on timing -- and writes C.
 template <bool kTA, bool kTB, Beta kBeta, Src kSrc>
-__global__ void __launch_bounds__(kThreads, 1) sgemmTileKernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(kThreads, 1) sgemmKernel(const __grid_constant__ GemmParams p) {
   using P = Plan<kTA, kTB, kSrc>;
   extern __shared__ unsigned char smem_raw[];
+  __shared__ int last_arrival;
+  __shared__ Cursor cursor[2];
   // Align within the shared window by offsetting smem_raw itself: pointers
   // derived from the __shared__ array stay in the shared address space, so the
   // compiler emits 32-bit shared loads (a uintptr_t round trip would turn them
@@ -229,10 +297,14 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmTileKernel(const __grid_cons
   auto stageA = [&](int s) { return P::kPairIsA ? stageP(s) : stageD(s); };
   auto stageB = [&](int s) { return P::kPairIsA ? stageD(s) : stageP(s); };
 
-  int tile_m, tile_n;
-  rasterTile(p, blockIdx.x, &tile_m, &tile_n);
-  const int m0 = tile_m * P::kBM, n0 = tile_n * P::kBN;
-  const int kiters = (p.k + kBK - 1) / kBK;
+  const int cta = blockIdx.x;
+  const int nitems = numItems(p, cta);
+  if (nitems == 0) return;  // whole CTA, before any barrier
+  int total = 0;            // k iterations over all items
+  for (int i = 0; i < nitems; ++i) {
+    const Item it = itemAt(p, cta, i);
+    total += it.ke - it.kb;
+  }
 
   const int tid = threadIdx.x;
   const int warp = tid / 32, lane = tid % 32;
@@ -257,6 +329,12 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmTileKernel(const __grid_cons
     return P::kD == Layout::kXK ? d_row0 + (j & 3) + 16 * (j >> 2) : d_row0 + 8 * j;
   };
   auto pCoord = [&](int i) { return p_base + (i & 3) + 32 * (i >> 2); };
+  auto origin = [&](int tile, int *m0, int *n0) {
+    int tm, tn;
+    rasterTile(p, tile, &tm, &tn);
+    *m0 = tm * P::kBM;
+    *n0 = tn * P::kBN;
+  };
 
   if constexpr (kSrc == Src::kTma) {
     if (tid == 0) {
@@ -269,31 +347,51 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmTileKernel(const __grid_cons
     __syncthreads();
   }
 
-  auto issue = [&](int kt) {
-    const int s = kt % kStages;
-    const int k0 = kt * kBK;
+  // Producer cursor: the next k iteration to stage. It lives in shared
+  // memory, double buffered: at flat iteration g every thread reads slot g%2
+  // and thread 0 writes the advanced cursor into the other slot, which nobody
+  // reads before the next barrier. (Keeping it in registers costs ~20 of them
+  // in a kernel that needs all it has for accumulators.)
+  if (tid == 0) {
+    const Item it = itemAt(p, cta, 0);
+    int m0, n0;
+    origin(it.tile, &m0, &n0);
+    cursor[0] = Cursor{0, it.kb, it.ke, m0, n0};
+  }
+  __syncthreads();
+  auto issue = [&](int i) {  // stage flat iteration i
+    const Cursor cur = cursor[i & 1];
+    const int s = i % kStages;
+    const int k0 = cur.kt * kBK;
     if constexpr (kSrc == Src::kTma) {
-      mbarArriveExpectTx(&full[s], kStageBytes);
-      if (P::kA == Layout::kXK) tmaLoad2d(stageA(s), &p.tma_a, &full[s], m0, k0);
-      else tmaLoad2d(stageA(s), &p.tma_a, &full[s], k0, m0);
-      if (P::kB == Layout::kXK) tmaLoad2d(stageB(s), &p.tma_b, &full[s], n0, k0);
-      else tmaLoad2d(stageB(s), &p.tma_b, &full[s], k0, n0);
+      if (tid == 0) {
+        mbarArriveExpectTx(&full[s], kStageBytes);
+        if (P::kA == Layout::kXK) tmaLoad2d(stageA(s), &p.tma_a, &full[s], cur.m0, k0);
+        else tmaLoad2d(stageA(s), &p.tma_a, &full[s], k0, cur.m0);
+        if (P::kB == Layout::kXK) tmaLoad2d(stageB(s), &p.tma_b, &full[s], cur.n0, k0);
+        else tmaLoad2d(stageB(s), &p.tma_b, &full[s], k0, cur.n0);
+      }
     } else {
-      copyTile<kTA, kTB>(p, stageA(s), stageB(s), m0, n0, k0);
+      copyTile<kTA, kTB>(p, stageA(s), stageB(s), cur.m0, cur.n0, k0);
+    }
+    if (tid == 0) {
+      Cursor nxt = cur;
+      if (++nxt.kt == cur.ke && ++nxt.idx < nitems) {
+        const Item it = itemAt(p, cta, nxt.idx);
+        nxt.kt = it.kb;
+        nxt.ke = it.ke;
+        origin(it.tile, &nxt.m0, &nxt.n0);
+      }
+      cursor[(i + 1) & 1] = nxt;
     }
   };
 
   // Prologue: fill kStages-1 stages.
-  if constexpr (kSrc == Src::kTma) {
-    if (tid == 0) {
-      for (int kt = 0; kt < kStages - 1 && kt < kiters; ++kt) issue(kt);
-    }
-  } else {
-#pragma unroll
-    for (int kt = 0; kt < kStages - 1; ++kt) {
-      if (kt < kiters) issue(kt);
-      cpAsyncCommit();
-    }
+#pragma unroll 1
+  for (int i = 0; i < kStages - 1; ++i) {
+    if (i < total) issue(i);
+    if constexpr (kSrc == Src::kCopy) cpAsyncCommit();
+    __syncthreads();  // the cursor slot written by thread 0 becomes visible
   }
 
   float2 acc[kTP / 2][kTD];
@@ -302,71 +400,142 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmTileKernel(const __grid_cons
 #pragma unroll
     for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
 
+  const float alpha = p.alpha, beta = p.beta;
+  // C = alpha * acc (+ beta * C) for the tile at (m0, n0).
+  auto storeTile = [&](int m0, int n0) {
+    if constexpr (P::kPairIsA) {
+      const bool vec = m0 + P::kBM <= p.m && n0 + P::kBN <= p.n && (p.ldc % 4 == 0) &&
+                       (reinterpret_cast<uintptr_t>(p.c) % 16 == 0);
+      if (vec) {
+#pragma unroll
+        for (int j = 0; j < kTD; ++j) {
+          float *col = p.c + static_cast<size_t>(n0 + dCoord(j)) * p.ldc + m0 + p_base;
+#pragma unroll
+          for (int q = 0; q < kTP / 4; ++q) {
+            const float2 lo = acc[2 * q][j], hi = acc[2 * q + 1][j];
+            float4 cv = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+            if constexpr (kBeta != Beta::kZero) cv = *reinterpret_cast<const float4 *>(col + 32 * q);
+            float4 out;
+            out.x = epilogueValue<kBeta>(lo.x, alpha, beta, cv.x);
+            out.y = epilogueValue<kBeta>(lo.y, alpha, beta, cv.y);
+            out.z = epilogueValue<kBeta>(hi.x, alpha, beta, cv.z);
+            out.w = epilogueValue<kBeta>(hi.y, alpha, beta, cv.w);
+            *reinterpret_cast<float4 *>(col + 32 * q) = out;
+          }
+        }
+        return;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kTD; ++j) {
+#pragma unroll
+      for (int i = 0; i < kTP; ++i) {
+        const int row = P::kPairIsA ? m0 + pCoord(i) : m0 + dCoord(j);
+        const int col = P::kPairIsA ? n0 + dCoord(j) : n0 + pCoord(i);
+        if (row < p.m && col < p.n) {
+          float *cp = p.c + static_cast<size_t>(col) * p.ldc + row;
+          const float a = (i & 1) ? acc[i >> 1][j].y : acc[i >> 1][j].x;
+          const float cv = kBeta == Beta::kZero ? 0.0F : *cp;
+          *cp = epilogueValue<kBeta>(a, alpha, beta, cv);
+        }
+      }
+    }
+  };
+
+  // Workspace slot layout: float4 e (0..31) of thread tid at slot[e * kThreads + tid].
+  auto publish = [&](int slot) {
+    float4 *w = p.ws + static_cast<size_t>(slot) * (kThreads * 32) + tid;
+#pragma unroll
+    for (int i = 0; i < kTP / 2; ++i)
+#pragma unroll
+      for (int j = 0; j < kTD; j += 2)
+        __stcg(w + (i * 4 + j / 2) * kThreads,
+               make_float4(acc[i][j].x, acc[i][j].y, acc[i][j + 1].x, acc[i][j + 1].y));
+  };
+  auto gather = [&](int slot) {
+    const float4 *w = p.ws + static_cast<size_t>(slot) * (kThreads * 32) + tid;
+#pragma unroll
+    for (int i = 0; i < kTP / 2; ++i)
+#pragma unroll
+      for (int j = 0; j < kTD; j += 2) {
+        const float4 v = __ldcg(w + (i * 4 + j / 2) * kThreads);
+        acc[i][j].x += v.x;
+        acc[i][j].y += v.y;
+        acc[i][j + 1].x += v.z;
+        acc[i][j + 1].y += v.w;
+      }
+  };
+
+  int c_idx = 0;
+  int c_kt, c_ke;
+  {
+    const Item it = itemAt(p, cta, 0);
+    c_kt = it.kb;
+    c_ke = it.ke;
+  }
   bool alive = true;
-  for (int kt = 0; kt < kiters; ++kt) {
-    const int s = kt % kStages;
+  for (int g = 0; g < total; ++g) {
+    const int s = g % kStages;
     if constexpr (kSrc == Src::kTma) {
-      const bool landed = mbarWait(&full[s], (kt / kStages) & 1, p.err);
+      const bool landed = mbarWait(&full[s], (g / kStages) & 1, p.err);
       // The barrier doubles as a vote, so that a timed-out wait stops the
       // whole CTA together instead of stranding the others at a barrier; it
-      // also means every warp is done with tile kt-1, whose stage is free.
+      // also means every warp is done with iteration g-1, whose stage is free.
       if (!__syncthreads_and(landed)) {
         alive = false;
         break;
       }
-      if (tid == 0 && kt + kStages - 1 < kiters) issue(kt + kStages - 1);
+      if (g + kStages - 1 < total) issue(g + kStages - 1);
     } else {
       cpAsyncWait<kStages - 2>();
       __syncthreads();
-      if (kt + kStages - 1 < kiters) issue(kt + kStages - 1);
+      if (g + kStages - 1 < total) issue(g + kStages - 1);
       cpAsyncCommit();
     }
     computeStage<P::kD>(stageP(s), stageD(s), p_base, da, acc);
-  }
-  if constexpr (kSrc == Src::kCopy) cpAsyncWait<0>();
-  if (!alive) return;
 
-  // ---- epilogue ----
-  // Element (i, j) of the thread's block: pair coordinate pCoord(i), i = 0..15,
-  // broadcast coordinate dCoord(j), j = 0..7; acc[i/2][j] holds (i even, i odd).
-  const float alpha = p.alpha, beta = p.beta;
-  if constexpr (P::kPairIsA) {
-    const bool vec = m0 + P::kBM <= p.m && n0 + P::kBN <= p.n && (p.ldc % 4 == 0) &&
-                     (reinterpret_cast<uintptr_t>(p.c) % 16 == 0);
-    if (vec) {
+    if (++c_kt == c_ke) {
+      const Item c_item = itemAt(p, cta, c_idx);
+      int c_m0, c_n0;
+      origin(c_item.tile, &c_m0, &c_n0);
+      if (c_item.kb == 0 && c_item.ke == p.kiters) {
+        storeTile(c_m0, c_n0);
+      } else {
+        // Stream-K piece: publish, count the arrival, and let the last
+        // arriving piece reduce all pieces in piece order.
+        const int u = c_item.tile - p.dp_tiles;
+        const int first = skOwner(p, u * p.kiters);
+        const int last = skOwner(p, (u + 1) * p.kiters - 1);
+        publish(skSlot(p, cta, u));
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) last_arrival = atomicAdd(p.counters + u, 1) == last - first;
+        __syncthreads();
+        if (last_arrival) {
+          __threadfence();
 #pragma unroll
-      for (int j = 0; j < kTD; ++j) {
-        float *col = p.c + static_cast<size_t>(n0 + dCoord(j)) * p.ldc + m0 + p_base;
+          for (int i = 0; i < kTP / 2; ++i)
 #pragma unroll
-        for (int q = 0; q < kTP / 4; ++q) {
-          const float2 lo = acc[2 * q][j], hi = acc[2 * q + 1][j];
-          float4 cv = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
-          if constexpr (kBeta != Beta::kZero) cv = *reinterpret_cast<const float4 *>(col + 32 * q);
-          float4 out;
-          out.x = epilogueValue<kBeta>(lo.x, alpha, beta, cv.x);
-          out.y = epilogueValue<kBeta>(lo.y, alpha, beta, cv.y);
-          out.z = epilogueValue<kBeta>(hi.x, alpha, beta, cv.z);
-          out.w = epilogueValue<kBeta>(hi.y, alpha, beta, cv.w);
-          *reinterpret_cast<float4 *>(col + 32 * q) = out;
+            for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
+#pragma unroll 1
+          for (int c = first; c <= last; ++c) gather(skSlot(p, c, u));
+          storeTile(c_m0, c_n0);
+          if (tid == 0) p.counters[u] = 0;  // ready for the next launch
         }
       }
-      return;
-    }
-  }
 #pragma unroll
-  for (int j = 0; j < kTD; ++j) {
+      for (int i = 0; i < kTP / 2; ++i)
 #pragma unroll
-    for (int i = 0; i < kTP; ++i) {
-      const int row = P::kPairIsA ? m0 + pCoord(i) : m0 + dCoord(j);
-      const int col = P::kPairIsA ? n0 + dCoord(j) : n0 + pCoord(i);
-      if (row < p.m && col < p.n) {
-        float *cp = p.c + static_cast<size_t>(col) * p.ldc + row;
-        const float a = (i & 1) ? acc[i >> 1][j].y : acc[i >> 1][j].x;
-        const float cv = kBeta == Beta::kZero ? 0.0F : *cp;
-        *cp = epilogueValue<kBeta>(a, alpha, beta, cv);
+        for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
+      if (++c_idx < nitems) {
+        const Item it = itemAt(p, cta, c_idx);
+        c_kt = it.kb;
+        c_ke = it.ke;
       }
     }
   }
+  if constexpr (kSrc == Src::kCopy) cpAsyncWait<0>();
+  (void)alive;
 }
 
 }  // namespace sgblas::kern

@@ -179,3 +179,50 @@ def test_parity_with_reference_library(cuda, handle):
         assert r_ref["ok_north_star"], ("reference outside the bound?", case.name, r_ref)
         _assert(r_us, case.name)
     ref.close()
+
+
+# ---- the persistent stream-K schedule -----------------------------------------
+# (m, n, k): one tile split over every SM; fewer tiles than SMs; a remainder
+# wave after whole waves; odd tails with many pieces per tile; K below the
+# split threshold.
+SK_SHAPES = [(256, 128, 65536), (512, 512, 4096), (1500, 1300, 3000), (2560, 1920, 1024),
+             (4096, 2048, 512), (300, 700, 100), (9472, 512, 384)]
+
+
+@pytest.mark.parametrize("m,n,k", SK_SHAPES)
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 1)])
+def test_stream_k_shapes(cuda, handle, m, n, k, ta, tb):
+    lda = k if ta else m
+    ldb = n if tb else k
+    case = C.Case("sk", ta, tb, m, n, k, lda, ldb, m, 0.5, -1.5)
+    a, b, c = C.cfg_inputs(case, m + n + k, None)
+    status, out = run_sgemm(cuda, handle, case, a, b, c)
+    assert status == 0
+    if m * n * k <= (1 << 31):
+        _assert(check_full(case, a, b, c, out), (m, n, k))
+    else:
+        _assert(check_sampled(case, a, b, c, out), (m, n, k))
+
+
+def test_workspace_shared_across_streams(cuda, handle):
+    """One handle alternating between two streams with no host sync between
+    calls: the workspace is ordered by an event, results are bit-identical to
+    a single-stream run."""
+    torch = cuda
+    case = C.Case("sk", 0, 0, 1500, 1300, 3000, 1500, 3000, 1500, 1.0, 0.0)
+    a, b, c = C.cfg_inputs(case, 77, None)
+    _, expect = run_sgemm(torch, handle, case, a, b, c)
+    da, pa = to_device(torch, a)
+    db, pb = to_device(torch, b)
+    outs = [torch.zeros(case.c_size, device="cuda") for _ in range(6)]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    torch.cuda.synchronize()
+    for i, o in enumerate(outs):
+        handle.set_stream(streams[i % 2])
+        handle.sgemm(0, 0, case.m, case.n, case.k, 1.0, pa, case.lda, pb, case.ldb, 0.0, o,
+                     case.ldc)
+    torch.cuda.synchronize()
+    handle.set_stream(None)
+    for o in outs:
+        assert np.array_equal(o.cpu().numpy(), expect)
+    assert sg.get_device_errors() == 0
