@@ -160,6 +160,9 @@ int smCount(int device) {
 }
 
 constexpr size_t kSlotBytes = size_t{kern::kThreads} * 32 * sizeof(float4);
+// Arrival counters: sk_tiles <= 2 * grid <= 2 * SMs, so 1024 counters cover
+// any GPU with up to 512 SMs.
+constexpr size_t kCounterRegionBytes = 4096;
 
 // Grow-only, stream-ordered workspace of the handle: [counters | slots].
 // Returns false (and the caller falls back to whole-tile scheduling) when it
@@ -222,8 +225,12 @@ sgblasStatus_t launchTiles(GemmParams p, sgblasContext *ctx, int device, cudaStr
   if (sms <= 0) return SGBLAS_STATUS_EXECUTION_FAILED;
   Schedule s = makeSchedule(tiles, p.kiters, sms);
   if (s.sk_tiles > 0) {
-    const size_t counter_bytes = (static_cast<size_t>(s.sk_tiles) * sizeof(int) + 255) & ~size_t{255};
-    if (ensureWorkspace(ctx, counter_bytes, 2 * static_cast<size_t>(s.grid) * kSlotBytes, device,
+    // The counter region has a fixed size so that the layout of the workspace
+    // is the same for every call: counters left at zero by one launch must not
+    // be overlapped by another launch's partial slots.
+    const size_t counter_bytes = kCounterRegionBytes;
+    if (static_cast<size_t>(s.sk_tiles) * sizeof(int) <= counter_bytes &&
+        ensureWorkspace(ctx, counter_bytes, 2 * static_cast<size_t>(s.grid) * kSlotBytes, device,
                         stream)) {
       p.counters = static_cast<int *>(ctx->workspace);
       p.ws = reinterpret_cast<float4 *>(static_cast<char *>(ctx->workspace) + counter_bytes);

@@ -226,3 +226,18 @@ def test_workspace_shared_across_streams(cuda, handle):
     for o in outs:
         assert np.array_equal(o.cpu().numpy(), expect)
     assert sg.get_device_errors() == 0
+
+
+def test_one_handle_many_stream_k_shapes(cuda, handle):
+    """One handle, successive problems whose stream-K schedules split
+    different numbers of tiles: the workspace layout must not move between
+    calls (counters zeroed by one launch stay zero for the next)."""
+    torch = cuda
+    shapes = [(1500, 1300, 3000), (4096, 2048, 512), (512, 512, 4096), (4096, 2048, 512),
+              (1500, 1300, 3000)]
+    for i, (m, n, k) in enumerate(shapes):
+        case = C.Case("reuse", 0, 1, m, n, k, m, n, m, 1.0, 0.0)
+        a, b, c = C.cfg_inputs(case, 900 + i, None)
+        status, out = run_sgemm(torch, handle, case, a, b, c)
+        assert status == 0
+        _assert(check_sampled(case, a, b, c, out, count=8192, seed=i), (i, m, n, k))
