@@ -17,6 +17,26 @@ extern "C" {
  * No counterpart in the reference (it has no device-side waits). */
 sgblasStatus_t sgblasGetDeviceErrors(unsigned *flags, int clear);
 
+/* sgblasSgemm for callers that cannot allocate device memory (their process
+ * or host owns the allocator, or forbids allocation after start-up). Same
+ * arguments, semantics and status codes as sgblasSgemm, but instead of the
+ * handle's lazily allocated workspace it uses one fixed 38 MiB scratch array
+ * built into the library, which every GPU that loads the library holds until
+ * exit. It never calls cudaMalloc, cudaFree or any allocating routine.
+ *   - The first call on a device resolves the scratch address; make it
+ *     before any stream capture.
+ *   - All calls on a device share the scratch and it keeps the last call's
+ *     contents: calls that may overlap on the GPU race, so order them.
+ *   - A schedule that needs more scratch than 38 MiB (only possible on a GPU
+ *     with more than 151 SMs) returns SGBLAS_STATUS_NOT_SUPPORTED.
+ * No counterpart in the reference API (the reference allocates nothing in
+ * the first place: it has no split-k workspace). */
+sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperation_t transa,
+                                  sgblasOperation_t transb, int m, int n, int k,
+                                  const float *alpha, const float *a, int lda,
+                                  const float *b, int ldb, const float *beta,
+                                  float *c, int ldc);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

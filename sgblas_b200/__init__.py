@@ -57,6 +57,11 @@ _SIGNATURES = {
                                     ctypes.c_void_p, ctypes.c_int]),
     "sgblasGetStatusString": (ctypes.c_char_p, [ctypes.c_int]),
     "sgblasGetDeviceErrors": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]),
+    "sgblasSgemmNoAlloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                           ctypes.c_int, ctypes.c_int, ctypes.c_int, _c_float_p,
+                                           ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                           ctypes.c_int, _c_float_p, ctypes.c_void_p,
+                                           ctypes.c_int]),
     # multi-GPU extension (include/sgblas/sgblas_mg.h)
     "sgblasMgGetUniqueId": (ctypes.c_int, [ctypes.c_void_p]),
     "sgblasMgCreate": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
