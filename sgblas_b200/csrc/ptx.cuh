@@ -62,6 +62,35 @@ __device__ __forceinline__ bool mbarWait(uint64_t *bar, uint32_t parity, unsigne
   return false;
 }
 
+// Plain arrive (release semantics at CTA scope).
+__device__ __forceinline__ void mbarArrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smemAddr(bar)) : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed.
+__device__ __forceinline__ void cpAsyncArrive(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smemAddr(bar))
+               : "memory");
+}
+
+// Named barrier over the first `count` threads of the CTA (id 0 is
+// __syncthreads).
+template <int kId, int kCount>
+__device__ __forceinline__ void namedBarrier() {
+  asm volatile("bar.sync %0, %1;" ::"n"(kId), "n"(kCount) : "memory");
+}
+
+// Warpgroup register reallocation (all 128 threads of the warpgroup execute
+// it). The block's launch allocation bounds the sum over warpgroups.
+template <int kRegs>
+__device__ __forceinline__ void regAlloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <int kRegs>
+__device__ __forceinline__ void regDealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 // 2-D TMA tile load global -> shared, completion signalled on `bar`.
 // x is the innermost (contiguous) coordinate in elements.
 __device__ __forceinline__ void tmaLoad2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x,

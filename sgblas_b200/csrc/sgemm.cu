@@ -159,7 +159,7 @@ int smCount(int device) {
   return v;
 }
 
-constexpr size_t kSlotBytes = size_t{kern::kThreads} * 32 * sizeof(float4);
+constexpr size_t kSlotBytes = size_t{kern::kThreads} * kern::kSlotFloat4 * sizeof(float4);
 // Arrival counters: sk_tiles <= 2 * grid <= 2 * SMs, so 1024 counters cover
 // any GPU with up to 512 SMs.
 constexpr size_t kCounterRegionBytes = 4096;
@@ -247,7 +247,7 @@ sgblasStatus_t launchTiles(GemmParams p, sgblasContext *ctx, int device, cudaStr
   p.sk_r = s.sk_r;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(s.grid));
-  cfg.blockDim = dim3(kern::kThreads);
+  cfg.blockDim = dim3(kern::kBlockThreads);
   cfg.dynamicSmemBytes = kern::kSmemBytes;
   cfg.stream = stream;
   const sgblasStatus_t st = launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));

@@ -48,7 +48,7 @@ using sgblas::kern::Src;
 // counters of up to 1024 split tiles and two 128 KiB partial slots for each of
 // up to 151 persistent CTAs (one per SM).
 constexpr size_t kCounterBytes = 4096;
-constexpr size_t kSlotBytes = size_t{sgblas::kern::kThreads} * 32 * sizeof(float4);
+constexpr size_t kSlotBytes = size_t{sgblas::kern::kThreads} * sgblas::kern::kSlotFloat4 * sizeof(float4);
 constexpr size_t kScratchBytes = size_t{38} << 20;
 
 }  // namespace
@@ -176,7 +176,7 @@ sgblasStatus_t launch(GemmParams p, int device, cudaStream_t stream) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.grid));
-  cfg.blockDim = dim3(sgblas::kern::kThreads);
+  cfg.blockDim = dim3(sgblas::kern::kBlockThreads);
   cfg.dynamicSmemBytes = sgblas::kern::kSmemBytes;
   cfg.stream = stream;
   return launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));

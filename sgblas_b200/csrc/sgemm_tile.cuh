@@ -23,15 +23,20 @@
 //   kKX : [BX][BK] floats, k contiguous, 64-byte rows with the TMA 64B swizzle
 //         (16-byte chunk index ^= (row >> 1) & 3).
 //
-// CTA tile: 256 (P) x 128 (D), 256 threads = 8 warps, one CTA per SM; each
-// thread owns a 16 (P) x 8 (D) block of C (64 FFMA2 per k step against 4+2
-// shared loads). Warps form 2 (P) x 4 (D); lane bits lp = lane % 8,
-// ld = lane / 8.
-//   P coordinates: 128*wp + 4*lp + {0..3} + 32*q, q = 0..3.
-//   D coordinates, kXK D tile: 32*wd + 4*ld + {0..3} + {0, 16}.
-//   D coordinates, kKX D tile: 64*(wd/2) + 4*(wd%2) + ld + 8*j, j = 0..7 --
-//     all eight rows of a thread share one swizzle phase ((row >> 1) & 3), and
-//     the four rows a warp reads together fall in four distinct bank groups.
+// CTA: three warpgroups, one CTA per SM.
+//   - Warpgroups 0-1 (256 threads, 8 warps) compute a 256 (P) x 128 (D) tile;
+//     each thread owns a 16 (P) x 8 (D) block of C (64 FFMA2 per k step against
+//     4+2 shared loads). Warps form 2 (P) x 4 (D); lane bits lp = lane % 8,
+//     ld = lane / 8.
+//       P coordinates: 128*wp + 4*lp + {0..3} + 32*q, q = 0..3.
+//       D coordinates ([k][x] tile): 32*wd + 4*ld + {0..3} + {0, 16}.
+//   - Warpgroup 2 (128 threads) is the producer: one thread issues the TMA
+//     tile loads (or all 128 issue cp.async copies), and all 128 transpose
+//     [x][k] broadcast tiles into [k][x] buffers. It gives registers to the
+//     compute warpgroups (setmaxnreg), so that those keep 232.
+//   Producer and consumers meet only at mbarriers (stage full/empty,
+//   transposed buffer full/empty), so no warp ever waits on a CTA-wide
+//   barrier inside the main loop.
 #ifndef SGBLAS_B200_SGEMM_TILE_CUH_
 #define SGBLAS_B200_SGEMM_TILE_CUH_
 
@@ -46,17 +51,34 @@ constexpr int kBP = 256;   // pair-operand tile extent
 constexpr int kBD = 128;   // broadcast-operand tile extent
 constexpr int kBK = 16;    // k slice per pipeline stage
 constexpr int kStages = 6;
-constexpr int kThreads = 256;
-constexpr int kTP = 16;    // pair-operand elements per thread
-constexpr int kTD = 8;     // broadcast-operand elements per thread
+constexpr int kTransBufs = 3;   // ring of transposed [k][x] broadcast tiles
+constexpr int kTP = 16;         // pair-operand elements per thread
+constexpr int kTD = 8;          // broadcast-operand elements per thread
+constexpr int kWarpsP = kBP / (8 * kTP);   // warps along P (8 lanes x kTP each)
+constexpr int kWarpsD = kBD / 32;          // warps along D (4 lanes x 8 each)
+constexpr int kThreads = 32 * kWarpsP * kWarpsD;   // compute threads (256)
+constexpr int kConsumerWarps = kThreads / 32;
+constexpr int kProducerThreads = 128;               // one warpgroup
+constexpr int kBlockThreads = kThreads + kProducerThreads;
+// Register split: the block is launched with kLaunchRegs per thread (what
+// __launch_bounds__(384, 1) leaves ptxas); setmaxnreg then moves registers
+// from the producer warpgroup to the compute warpgroups.
+constexpr int kLaunchRegs = 168;
+constexpr int kConsumerRegs = 232;
+constexpr int kProducerRegs = 40;
+static_assert(kThreads * kConsumerRegs + kProducerThreads * kProducerRegs <=
+                  kBlockThreads * kLaunchRegs,
+              "register split exceeds the launch allocation");
+constexpr int kSlotFloat4 = kTP * kTD / 4;  // float4s per thread in a partial slot
 constexpr int kPairFloats = kBP * kBK;
 constexpr int kDupFloats = kBD * kBK;
 constexpr int kPairBytes = kPairFloats * 4;   // 16 KiB
 constexpr int kDupBytes = kDupFloats * 4;     // 8 KiB
 constexpr int kStageBytes = kPairBytes + kDupBytes;
-constexpr int kTransBytes = 2 * kDupBytes;     // two [k][x] copies of a broadcast tile
+constexpr int kTransBytes = kTransBufs * kDupBytes;
+constexpr int kBarrierBytes = 8 * (2 * kStages + 2 * kTransBufs);
 constexpr int kSmemAlign = 1024;
-constexpr int kSmemBytes = kStages * kStageBytes + kTransBytes + 256 + kSmemAlign;
+constexpr int kSmemBytes = kStages * kStageBytes + kTransBytes + kBarrierBytes + kSmemAlign;
 
 enum class Beta { kZero, kOne, kGeneral };
 enum class Src { kTma, kCopy };
@@ -83,7 +105,7 @@ struct GemmParams {
   int dp_tiles;
   int sk_tiles;
   int sk_q, sk_r;
-  float4 *ws;         // 2 * grid partial-tile slots of kThreads * 32 float4
+  float4 *ws;         // 2 * grid partial-tile slots of kThreads * kSlotFloat4 float4
   int *counters;      // sk_tiles arrival counters, zero between launches
 };
 
@@ -92,10 +114,6 @@ struct Item {
   int tile, kb, ke;
 };
 
-// Producer position: item index, k iteration, item end, tile origin.
-struct Cursor {
-  int idx, kt, ke, m0, n0;
-};
 
 __device__ __forceinline__ int skBegin(const GemmParams &p, int c) {
   return c * p.sk_q + min(c, p.sk_r);
@@ -176,11 +194,11 @@ __device__ __forceinline__ void rasterTile(const GemmParams &p, int t, int *tm, 
 // reads are coalesced along each operand's contiguous dimension.
 template <bool kTA, bool kTB>
 __device__ __forceinline__ void copyTile(const GemmParams &p, float *sa, float *sb, int m0, int n0,
-                                         int k0) {
-  const int tid = threadIdx.x;
-#pragma unroll
-  for (int r = 0; r < kPairFloats / kThreads; ++r) {
-    const int e = tid + r * kThreads;
+                                         int k0, int tid) {
+  constexpr int kN = kProducerThreads;
+#pragma unroll 4
+  for (int r = 0; r < kPairFloats / kN; ++r) {
+    const int e = tid + r * kN;
     const int mm = kTA ? e / kBK : e % kBP;
     const int kk = kTA ? e % kBK : e / kBP;
     const int gm = m0 + mm, gk = k0 + kk;
@@ -192,9 +210,9 @@ __device__ __forceinline__ void copyTile(const GemmParams &p, float *sa, float *
     }
     cpAsync4(sa + kk * kBP + mm, src, ok ? 4u : 0u);
   }
-#pragma unroll
-  for (int r = 0; r < kDupFloats / kThreads; ++r) {
-    const int e = tid + r * kThreads;
+#pragma unroll 4
+  for (int r = 0; r < kDupFloats / kN; ++r) {
+    const int e = tid + r * kN;
     const int nn = kTB ? e % kBD : e / kBK;
     const int kk = kTB ? e / kBD : e % kBK;
     const int gn = n0 + nn, gk = k0 + kk;
@@ -216,25 +234,23 @@ struct DupAddr {
   uint32_t chunk[4];    // kKX: swizzled byte offset of each 16-byte k chunk
 };
 
-// [x][k] broadcast tile (64-byte swizzled rows) -> [k][x] (kBD floats per k):
-// thread t moves row t % kBD, k half t / kBD. Reads are conflict-free thanks
-// to the swizzle, writes are 32 consecutive floats per warp.
+// [x][k] broadcast tile (64-byte swizzled rows) -> [k][x] (kBD floats per k),
+// by the producer warpgroup: thread t moves row t. A warp reads 32
+// consecutive rows at one chunk -- conflict-free thanks to the swizzle -- and
+// writes 32 consecutive floats per k.
 __device__ __forceinline__ void transposeDup(const float *src, float *dst, int tid) {
-  static_assert(kThreads == 2 * kBD && kBK == 16, "one row half per thread");
-  const int x = tid % kBD, kh = tid / kBD;
-  const char *row = reinterpret_cast<const char *>(src) + x * 64;
-  const int phase = (x >> 1) & 3;
-  const float4 v0 = *reinterpret_cast<const float4 *>(row + (((2 * kh) ^ phase) << 4));
-  const float4 v1 = *reinterpret_cast<const float4 *>(row + (((2 * kh + 1) ^ phase) << 4));
-  float *d = dst + 8 * kh * kBD + x;
-  d[0 * kBD] = v0.x;
-  d[1 * kBD] = v0.y;
-  d[2 * kBD] = v0.z;
-  d[3 * kBD] = v0.w;
-  d[4 * kBD] = v1.x;
-  d[5 * kBD] = v1.y;
-  d[6 * kBD] = v1.z;
-  d[7 * kBD] = v1.w;
+  static_assert(kProducerThreads == kBD && kBK == 16, "one row per producer thread");
+  const char *row = reinterpret_cast<const char *>(src) + tid * 64;
+  const int phase = (tid >> 1) & 3;
+  float *d = dst + tid;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float4 v = *reinterpret_cast<const float4 *>(row + ((c ^ phase) << 4));
+    d[(4 * c + 0) * kBD] = v.x;
+    d[(4 * c + 1) * kBD] = v.y;
+    d[(4 * c + 2) * kBD] = v.z;
+    d[(4 * c + 3) * kBD] = v.w;
+  }
 }
 
 // ---- the FFMA2 micro-kernel over one BK slice ------------------------------
@@ -294,20 +310,30 @@ __device__ __forceinline__ float epilogueValue(float acc, float alpha, float bet
   }
 }
 
-// ---- the persistent kernel ----------------------------------------------------
+// ---- the persistent, warp-specialized kernel ----------------------------------
 // Each CTA walks its items in order (whole tiles first, then its stream-K
-// range). The k iterations of consecutive items form one flat stream, so the
-// stage ring keeps prefetching the next tile while the current one finishes.
-// A stream-K piece that does not cover its whole tile is published to the
-// workspace; the CTA that publishes the last piece of a tile (an atomic
-// arrival count, no waiting) sums every piece in piece order -- the order is
-// fixed by the schedule, so results do not depend on timing -- and writes C.
+// range); the k iterations of consecutive items form one flat stream, so the
+// producer keeps prefetching the next tile while the compute warps finish the
+// current one. A stream-K piece that does not cover its whole tile is
+// published to the workspace; the CTA that publishes the last piece of a tile
+// (an atomic arrival count, no waiting) sums every piece in piece order -- an
+// order fixed by the schedule, so results do not depend on timing -- and
+// writes C.
+//
+// Synchronisation (all mbarriers, all waits bounded):
+//   full[s]     stage s holds iteration i's tiles   (TMA bytes / cp.async)
+//   empty[s]    the 8 compute warps are done with stage s's pair tile
+//   tfull[t]    transposed broadcast buffer t is written (128 producer threads)
+//   tempty[t]   the 8 compute warps are done with buffer t
+// A wait that times out raises the device error flag; from then on that
+// thread skips its waits (results are garbage and flagged) but still runs
+// every loop to its end, so that no thread is left behind at a barrier.
 template <bool kTA, bool kTB, Beta kBeta, Src kSrc>
-__global__ void __launch_bounds__(kThreads, 1) sgemmKernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(kBlockThreads, 1)
+    sgemmKernel(const __grid_constant__ GemmParams p) {
   using P = Plan<kTA, kTB, kSrc>;
   extern __shared__ unsigned char smem_raw[];
   __shared__ int last_arrival;
-  __shared__ Cursor cursor[2];
   // Align within the shared window by offsetting smem_raw itself: pointers
   // derived from the __shared__ array stay in the shared address space, so the
   // compiler emits 32-bit shared loads (a uintptr_t round trip would turn them
@@ -315,6 +341,9 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmKernel(const __grid_constant
   unsigned char *smem = smem_raw + ((kSmemAlign - (smemAddr(smem_raw) & (kSmemAlign - 1))) &
                                     (kSmemAlign - 1));
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes + kTransBytes);
+  uint64_t *empty = full + kStages;
+  uint64_t *tfull = empty + kStages;
+  uint64_t *tempty = tfull + kTransBufs;
   auto tbuf = [&](int i) {
     return reinterpret_cast<float *>(smem + kStages * kStageBytes + i * kDupBytes);
   };
@@ -325,6 +354,12 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmKernel(const __grid_constant
   };
   auto stageA = [&](int s) { return P::kPairIsA ? stageP(s) : stageD(s); };
   auto stageB = [&](int s) { return P::kPairIsA ? stageD(s) : stageP(s); };
+  auto origin = [&](int tile, int *m0, int *n0) {
+    int tm, tn;
+    rasterTile(p, tile, &tm, &tn);
+    *m0 = tm * P::kBM;
+    *n0 = tn * P::kBN;
+  };
 
   const int cta = blockIdx.x;
   const int nitems = numItems(p, cta);
@@ -334,94 +369,103 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmKernel(const __grid_constant
     const Item it = itemAt(p, cta, i);
     total += it.ke - it.kb;
   }
-
   const int tid = threadIdx.x;
-  const int warp = tid / 32, lane = tid % 32;
-  const int wp = warp % 2, wd = warp / 2;
-  const int lp = lane % 8, ld = lane / 8;
-  const int p_base = wp * 128 + lp * 4;
-  DupAddr da;
-  int d_row0;  // kKX: first row; kXK: first column
-  if constexpr (P::kCompD == Layout::kXK) {
-    d_row0 = wd * 32 + ld * 4;
-    da.base = static_cast<uint32_t>(d_row0);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) da.chunk[c] = 0;
-  } else {
-    d_row0 = (wd / 2) * 64 + (wd % 2) * 4 + ld;
-    da.base = static_cast<uint32_t>(d_row0 * 64);
-    const int phase = (d_row0 >> 1) & 3;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) da.chunk[c] = static_cast<uint32_t>((c ^ phase) << 4);
-  }
-  auto dCoord = [&](int j) {
-    return P::kCompD == Layout::kXK ? d_row0 + (j & 3) + 16 * (j >> 2) : d_row0 + 8 * j;
-  };
-  auto pCoord = [&](int i) { return p_base + (i & 3) + 32 * (i >> 2); };
-  auto origin = [&](int tile, int *m0, int *n0) {
-    int tm, tn;
-    rasterTile(p, tile, &tm, &tn);
-    *m0 = tm * P::kBM;
-    *n0 = tn * P::kBN;
-  };
 
-  if constexpr (kSrc == Src::kTma) {
-    if (tid == 0) {
+  if (tid == 0) {
+    if constexpr (kSrc == Src::kTma) {
       prefetchTensorMap(&p.tma_a);
       prefetchTensorMap(&p.tma_b);
-#pragma unroll
-      for (int s = 0; s < kStages; ++s) mbarInit(&full[s], 1);
-      fenceBarrierInit();
     }
-    __syncthreads();
-  }
-
-  // Producer cursor: the next k iteration to stage. It lives in shared
-  // memory, double buffered: at flat iteration g every thread reads slot g%2
-  // and thread 0 writes the advanced cursor into the other slot, which nobody
-  // reads before the next barrier. (Keeping it in registers costs ~20 of them
-  // in a kernel that needs all it has for accumulators.)
-  if (tid == 0) {
-    const Item it = itemAt(p, cta, 0);
-    int m0, n0;
-    origin(it.tile, &m0, &n0);
-    cursor[0] = Cursor{0, it.kb, it.ke, m0, n0};
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbarInit(&full[s], kSrc == Src::kTma ? 1 : kProducerThreads);
+      mbarInit(&empty[s], kConsumerWarps);
+    }
+#pragma unroll
+    for (int t = 0; t < kTransBufs; ++t) {
+      mbarInit(&tfull[t], kProducerThreads);
+      mbarInit(&tempty[t], kConsumerWarps);
+    }
+    fenceBarrierInit();
   }
   __syncthreads();
-  auto issue = [&](int i) {  // stage flat iteration i
-    const Cursor cur = cursor[i & 1];
-    const int s = i % kStages;
-    const int k0 = cur.kt * kBK;
-    if constexpr (kSrc == Src::kTma) {
-      if (tid == 0) {
-        mbarArriveExpectTx(&full[s], kStageBytes);
-        if (P::kA == Layout::kXK) tmaLoad2d(stageA(s), &p.tma_a, &full[s], cur.m0, k0);
-        else tmaLoad2d(stageA(s), &p.tma_a, &full[s], k0, cur.m0);
-        if (P::kB == Layout::kXK) tmaLoad2d(stageB(s), &p.tma_b, &full[s], cur.n0, k0);
-        else tmaLoad2d(stageB(s), &p.tma_b, &full[s], k0, cur.n0);
-      }
-    } else {
-      copyTile<kTA, kTB>(p, stageA(s), stageB(s), cur.m0, cur.n0, k0);
-    }
-    if (tid == 0) {
-      Cursor nxt = cur;
-      if (++nxt.kt == cur.ke && ++nxt.idx < nitems) {
-        const Item it = itemAt(p, cta, nxt.idx);
-        nxt.kt = it.kb;
-        nxt.ke = it.ke;
-        origin(it.tile, &nxt.m0, &nxt.n0);
-      }
-      cursor[(i + 1) & 1] = nxt;
-    }
-  };
 
-  // Prologue: fill kStages-1 stages.
-#pragma unroll 1
-  for (int i = 0; i < kStages - 1; ++i) {
-    if (i < total) issue(i);
-    if constexpr (kSrc == Src::kCopy) cpAsyncCommit();
-    __syncthreads();  // the cursor slot written by thread 0 becomes visible
+  // ======================= producer warpgroup ===============================
+  if (tid >= kThreads) {
+    regDealloc<kProducerRegs>();
+    const int pt = tid - kThreads;
+    bool ok = true;
+    auto wait = [&](uint64_t *bar, int parity) {
+      if (ok) ok = mbarWait(bar, static_cast<uint32_t>(parity), p.err);
+    };
+    int idx = 0, kt, ke, m0, n0;
+    {
+      const Item it = itemAt(p, cta, 0);
+      kt = it.kb;
+      ke = it.ke;
+      origin(it.tile, &m0, &n0);
+    }
+    // Transposes trail the loads by kLag iterations: far enough behind for the
+    // data to have landed, early enough to stay ahead of the compute warps.
+    constexpr int kLag = P::kTransD ? kStages - 2 : 0;
+    for (int i = 0; i < total + kLag; ++i) {
+      if (i < total) {
+        const int s = i % kStages;
+        const int k0 = kt * kBK;
+        if constexpr (kSrc == Src::kTma) {
+          if (pt == 0) {
+            if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
+            mbarArriveExpectTx(&full[s], kStageBytes);
+            if (P::kA == Layout::kXK) tmaLoad2d(stageA(s), &p.tma_a, &full[s], m0, k0);
+            else tmaLoad2d(stageA(s), &p.tma_a, &full[s], k0, m0);
+            if (P::kB == Layout::kXK) tmaLoad2d(stageB(s), &p.tma_b, &full[s], n0, k0);
+            else tmaLoad2d(stageB(s), &p.tma_b, &full[s], k0, n0);
+          }
+        } else {
+          if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
+          copyTile<kTA, kTB>(p, stageA(s), stageB(s), m0, n0, k0, pt);
+          cpAsyncArrive(&full[s]);
+        }
+        if (++kt == ke && ++idx < nitems) {
+          const Item it = itemAt(p, cta, idx);
+          kt = it.kb;
+          ke = it.ke;
+          origin(it.tile, &m0, &n0);
+        }
+      }
+      if constexpr (P::kTransD) {
+        const int j = i - kLag;
+        if (j >= 0) {
+          const int t = j % kTransBufs;
+          wait(&full[j % kStages], (j / kStages) & 1);
+          if (j >= kTransBufs) wait(&tempty[t], (j / kTransBufs - 1) & 1);
+          transposeDup(stageD(j % kStages), tbuf(t), pt);
+          mbarArrive(&tfull[t]);
+        }
+      }
+    }
+    if constexpr (kSrc == Src::kCopy) cpAsyncWait<0>();
+    return;
   }
+
+  // ======================= compute warpgroups ===============================
+  regAlloc<kConsumerRegs>();
+  const int warp = tid / 32, lane = tid % 32;
+  const int wp = warp % kWarpsP, wd = warp / kWarpsP;
+  const int lp = lane % 8, ld = lane / 8;
+  const int p_base = wp * (8 * kTP) + lp * 4;
+  DupAddr da;
+  const int d_row0 = wd * 32 + ld * 4;  // [k][x] broadcast tile: first column
+  da.base = static_cast<uint32_t>(d_row0);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) da.chunk[c] = 0;
+  static_assert(P::kCompD == Layout::kXK, "compute reads [k][x] broadcast tiles");
+  auto dCoord = [&](int j) { return d_row0 + (j & 3) + 16 * (j >> 2); };
+  auto pCoord = [&](int i) { return p_base + (i & 3) + 32 * (i >> 2); };
+  bool ok = true;
+  auto wait = [&](uint64_t *bar, int parity) {
+    if (ok) ok = mbarWait(bar, static_cast<uint32_t>(parity), p.err);
+  };
 
   float2 acc[kTP / 2][kTD];
 #pragma unroll
@@ -471,23 +515,23 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmKernel(const __grid_constant
     }
   };
 
-  // Workspace slot layout: float4 e (0..31) of thread tid at slot[e * kThreads + tid].
+  // Workspace slot layout: float4 e of thread tid at slot[e * kThreads + tid].
   auto publish = [&](int slot) {
-    float4 *w = p.ws + static_cast<size_t>(slot) * (kThreads * 32) + tid;
+    float4 *w = p.ws + static_cast<size_t>(slot) * (kThreads * kSlotFloat4) + tid;
 #pragma unroll
     for (int i = 0; i < kTP / 2; ++i)
 #pragma unroll
       for (int j = 0; j < kTD; j += 2)
-        __stcg(w + (i * 4 + j / 2) * kThreads,
+        __stcg(w + (i * (kTD / 2) + j / 2) * kThreads,
                make_float4(acc[i][j].x, acc[i][j].y, acc[i][j + 1].x, acc[i][j + 1].y));
   };
   auto gather = [&](int slot) {
-    const float4 *w = p.ws + static_cast<size_t>(slot) * (kThreads * 32) + tid;
+    const float4 *w = p.ws + static_cast<size_t>(slot) * (kThreads * kSlotFloat4) + tid;
 #pragma unroll
     for (int i = 0; i < kTP / 2; ++i)
 #pragma unroll
       for (int j = 0; j < kTD; j += 2) {
-        const float4 v = __ldcg(w + (i * 4 + j / 2) * kThreads);
+        const float4 v = __ldcg(w + (i * (kTD / 2) + j / 2) * kThreads);
         acc[i][j].x += v.x;
         acc[i][j].y += v.y;
         acc[i][j + 1].x += v.z;
@@ -502,44 +546,17 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmKernel(const __grid_constant
     c_kt = it.kb;
     c_ke = it.ke;
   }
-  bool alive = true;
-  // With a transposed broadcast tile, iteration g+1's tile is transposed
-  // during iteration g (before its compute), so the wait for a stage happens
-  // one iteration early; `ahead_ok` carries that wait's result into the next
-  // barrier vote.
-  bool ahead_ok = true;
-  auto transposeAhead = [&](int i) {  // make iteration i's broadcast tile [k][x]
-    bool ok = true;
-    if constexpr (kSrc == Src::kTma) {
-      ok = mbarWait(&full[i % kStages], (i / kStages) & 1, p.err);
-    } else {
-      cpAsyncWait<kStages - 2>();
-      __syncthreads();  // every thread's copies of iteration i have landed
-    }
-    if (ok) transposeDup(stageD(i % kStages), tbuf(i & 1), tid);
-    return ok;
-  };
-  if constexpr (P::kTransD) ahead_ok = transposeAhead(0);
   for (int g = 0; g < total; ++g) {
     const int s = g % kStages;
-    bool landed = ahead_ok;
-    if constexpr (!P::kTransD) {
-      if constexpr (kSrc == Src::kTma) landed = mbarWait(&full[s], (g / kStages) & 1, p.err);
-      else cpAsyncWait<kStages - 2>();
+    const int t = g % kTransBufs;
+    wait(&full[s], (g / kStages) & 1);
+    if constexpr (P::kTransD) wait(&tfull[t], (g / kTransBufs) & 1);
+    computeStage<P::kCompD>(stageP(s), P::kTransD ? tbuf(t) : stageD(s), p_base, da, acc);
+    __syncwarp();
+    if (lane == 0) {
+      mbarArrive(&empty[s]);
+      if constexpr (P::kTransD) mbarArrive(&tempty[t]);
     }
-    // The barrier doubles as a vote, so that a timed-out wait stops the whole
-    // CTA together instead of stranding the others at a barrier; it also
-    // means every warp is done with iteration g-1, whose stage is free.
-    if (!__syncthreads_and(landed)) {
-      alive = false;
-      break;
-    }
-    if (g + kStages - 1 < total) issue(g + kStages - 1);
-    if constexpr (kSrc == Src::kCopy) cpAsyncCommit();
-    if constexpr (P::kTransD) {
-      if (g + 1 < total) ahead_ok = transposeAhead(g + 1);
-    }
-    computeStage<P::kCompD>(stageP(s), P::kTransD ? tbuf(g & 1) : stageD(s), p_base, da, acc);
 
     if (++c_kt == c_ke) {
       const Item c_item = itemAt(p, cta, c_idx);
@@ -555,9 +572,9 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmKernel(const __grid_constant
         const int last = skOwner(p, (u + 1) * p.kiters - 1);
         publish(skSlot(p, cta, u));
         __threadfence();
-        __syncthreads();
+        namedBarrier<1, kThreads>();
         if (tid == 0) last_arrival = atomicAdd(p.counters + u, 1) == last - first;
-        __syncthreads();
+        namedBarrier<1, kThreads>();
         if (last_arrival) {
           __threadfence();
 #pragma unroll
@@ -581,8 +598,6 @@ __global__ void __launch_bounds__(kThreads, 1) sgemmKernel(const __grid_constant
       }
     }
   }
-  if constexpr (kSrc == Src::kCopy) cpAsyncWait<0>();
-  (void)alive;
 }
 
 }  // namespace sgblas::kern
