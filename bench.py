@@ -422,12 +422,12 @@ def e2e_single(torch, sg, ha, hb, m, n, k, steps, warmup) -> dict:
 def run_sharded(args) -> None:
     """N ranks: config 5, 32768 x 32768 x 8192 NN, columns split across ranks,
     A broadcast from rank 0 inside every step (sgblasMgSgemm)."""
-    import numpy as np
     import torch
     import torch.distributed as dist
     from datetime import timedelta
 
     import sgblas_b200 as sg
+    from sgblas_b200.mg import check_consistent, exchange_unique_id, shard_columns
 
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
@@ -437,13 +437,10 @@ def run_sharded(args) -> None:
     torch.cuda.set_device(local)
     dist.init_process_group("gloo", timeout=timedelta(seconds=300))
     M, N, K = 32768, 32768, 8192
-    assert N % world == 0
-    n_loc = N // world
+    _, n_loc = shard_columns(N, world, rank)
     flops = 2.0 * M * N * K
-
-    uid = [sg.mg_unique_id() if rank == 0 else None]
-    dist.broadcast_object_list(uid, src=0)
-    mg = sg.MgHandle(world, rank, uid[0], local)
+    check_consistent(dict(transa=0, transb=0, m=M, k=K, alpha=1.0, beta=0.0, lda=M, root=0))
+    mg = sg.MgHandle(world, rank, exchange_unique_id(sg.mg_unique_id), local)
     stream = torch.cuda.Stream()
     mg.set_stream(stream)
 
@@ -483,29 +480,94 @@ def run_sharded(args) -> None:
     clocks = clk.summary()
     allc = [None] * world
     dist.all_gather_object(allc, clocks)
+    errors = sg.get_device_errors()
+    del a, b, c
+    torch.cuda.empty_cache()
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_sharded(torch, dist, sg, mg, rank, M, n_loc, K, flops, max(2, steps // 2))
     mg.close()
     props = torch.cuda.get_device_properties(local)
     sms = props.multi_processor_count
     mhz = statistics.median([x["sm_mhz"] for x in allc if x["sm_mhz"]] or [1965.0])
     peak = world * fp32_peak_tflops(sms, mhz)
     if rank == 0:
+        if errors != 0:
+            raise RuntimeError("device error flags raised during the bench")
         reasons = sorted({r for x in allc for r in x["reasons"]})
         out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
                "warmup": warmup, "ms_per_step": 1e3 * total_s / steps, "higher_is_better": True,
                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                "config": {"workload": f"sharded sgemm NN {M}x{N}x{K} (BASELINE configs[4]), "
-                                      f"B and C split into {world} column blocks of {n_loc}, "
+                                      f"B and C split into {world} column blocks, "
                                       "A (1 GiB) broadcast from rank 0 by NCCL in every step",
+                          "m": M, "n": N, "k": K,
                           "parallelism": f"column-shard x{world}", "l2": "inputs larger than L2"},
                "roofline": {"bound": "fp32_fma", "achieved": value, "peak": peak, "unit": UNIT,
                             "frac": value / peak, "traffic": None,
-                            "peak_source": f"{world} x {sms} SMs x 128 lanes x 2 x {mhz:.0f} MHz"},
+                            "peak_source": f"{world} x {sms} SMs x 128 lanes x 2 x {mhz:.0f} MHz "
+                                           "(median sampled SM clock)"},
                "clocks": {"sm_mhz": mhz, "sm_max_mhz": max((x["sm_max_mhz"] or 0) for x in allc),
                           "reasons": reasons},
-               "gpu_launches": steps}
+               "gpu_launches": steps, "e2e": e2e}
         print(json.dumps(out), flush=True)
     dist.barrier()
     dist.destroy_process_group()
+
+
+def e2e_sharded(torch, dist, sg, mg, rank, M, n_loc, K, flops, steps) -> dict:
+    """Config 5 through the C ABI from host memory: every step rank 0 copies
+    A in, every rank copies its B shard in, runs sgblasMgSgemm and copies its
+    C shard out. Two buffer sets overlap the copies of step i+1 with step i."""
+    pa = torch.empty(M * K).uniform_(-1.0, 1.0).pin_memory() if rank == 0 else None
+    pb = torch.empty(K * n_loc).uniform_(-1.0, 1.0).pin_memory()
+    pc = torch.empty(M * n_loc).pin_memory()
+    sets = [(torch.empty(M * K, device="cuda"), torch.empty(K * n_loc, device="cuda"),
+             torch.empty(M * n_loc, device="cuda")) for _ in range(2)]
+    s_in, s_comp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    mg.set_stream(s_comp)
+    in_done = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+
+    def run(count):
+        for i in range(count):
+            j = i % 2
+            da, db, dc = sets[j]
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(comp_done[j])
+                if pa is not None:
+                    da.copy_(pa, non_blocking=True)
+                db.copy_(pb, non_blocking=True)
+                in_done[j].record(s_in)
+            s_comp.wait_event(in_done[j])
+            if i >= 2:
+                s_comp.wait_event(out_done[j])
+            mg.sgemm(0, 0, M, n_loc, K, 1.0, da, M, 0, db, K, 0.0, dc, M)
+            comp_done[j].record(s_comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(comp_done[j])
+                pc.copy_(dc, non_blocking=True)
+                out_done[j].record(s_out)
+
+    run(2)
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s_in)
+    run(steps)
+    s_in.wait_stream(s_out)
+    end.record(s_in)
+    torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(end) / 1e3], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {"value": flops * steps / float(t.item()) / 1e12, "unit": UNIT,
+            "h2d_bytes_per_step": 4 * (M * K + K * 32768), "d2h_bytes_per_step": 4 * M * 32768,
+            "steps": steps,
+            "pipelining": "2 buffer sets per rank; H2D, broadcast+SGEMM and D2H on 3 streams; "
+                          "bytes are whole-job totals (A once on rank 0, B and C over all ranks)"}
 
 
 def main():
