@@ -241,3 +241,23 @@ def test_one_handle_many_stream_k_shapes(cuda, handle):
         status, out = run_sgemm(torch, handle, case, a, b, c)
         assert status == 0
         _assert(check_sampled(case, a, b, c, out, count=8192, seed=i), (i, m, n, k))
+
+
+def test_matches_reference_golden_outputs(cuda, handle):
+    """Our outputs at the entries the reference library produced on a B200
+    (tests/golden/reference_suite.npz): both lie within the north-star bound
+    of the FP64 oracle, so they agree to within twice that bound."""
+    import pathlib
+
+    import oracle
+    from tests.golden.make_golden import golden_cases
+    gold = np.load(pathlib.Path(__file__).resolve().parent / "golden" / "reference_suite.npz")
+    for case, a, b, c in golden_cases():
+        rows, cols = gold[f"{case.name}/rows"], gold[f"{case.name}/cols"]
+        theirs = gold[f"{case.name}/vals"].astype(np.float64)
+        status, out = run_sgemm(cuda, handle, case, a, b, c)
+        assert status == 0
+        ours = out[rows.astype(np.int64) + cols.astype(np.int64) * case.ldc].astype(np.float64)
+        _, mag = oracle.sgemm_f64_points(case.transa, case.transb, case.k, case.alpha, a,
+                                         case.lda, b, case.ldb, case.beta, c, case.ldc, rows, cols)
+        assert np.all(np.abs(ours - theirs) <= 2 * oracle.tol_north_star(case.k, mag)), case.name
