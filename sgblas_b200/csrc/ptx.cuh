@@ -114,6 +114,17 @@ __device__ __forceinline__ void cpAsync4(void *dst, const void *src, uint32_t by
                : "memory");
 }
 
+// cp.async of kBytes (4, 8 or 16) with zero fill: copies `bytes` (<= kBytes)
+// and zero-fills the rest of the kBytes destination. Both addresses must be
+// kBytes-aligned.
+template <int kBytes>
+__device__ __forceinline__ void cpAsyncN(void *dst, const void *src, uint32_t bytes) {
+  static_assert(kBytes == 4 || kBytes == 8 || kBytes == 16, "cp.async size");
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;" ::"r"(smemAddr(dst)), "l"(src),
+               "n"(kBytes), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void cpAsyncCommit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 
 template <int N>

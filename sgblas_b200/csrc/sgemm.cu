@@ -8,9 +8,9 @@
 // error it caused itself (cudaLaunchKernelEx returns the launch's own status),
 // so an error the caller left pending is not swallowed.
 #include "context.hpp"
-#include "sgemm_tile.cuh"
-#include "validation.hpp"
 #include "device.hpp"
+#include "sgemm_launch.hpp"
+#include "validation.hpp"
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -22,9 +22,7 @@
 
 namespace sgblas::detail {
 
-using kern::Beta;
 using kern::GemmParams;
-using kern::Src;
 
 namespace {
 
@@ -43,11 +41,15 @@ __global__ void scaleKernel(int m, int n, float beta, float *c, int ldc) {
   }
 }
 
+}  // namespace
+
 sgblasStatus_t launchStatus(cudaError_t e) {
   if (e == cudaSuccess) return SGBLAS_STATUS_SUCCESS;
   (void)cudaGetLastError();  // clear the error this launch produced
   return SGBLAS_STATUS_EXECUTION_FAILED;
 }
+
+namespace {
 
 sgblasStatus_t launchScale(int m, int n, float beta, float *c, int ldc, cudaStream_t stream) {
   const unsigned row_blocks = static_cast<unsigned>((m + 255) / 256);
@@ -63,9 +65,13 @@ sgblasStatus_t launchScale(int m, int n, float beta, float *c, int ldc, cudaStre
   return launchStatus(e);
 }
 
+}  // namespace
+
 // ---------------------------------------------------------------------------
 // TMA descriptors. cuTensorMapEncodeTiled is a host-side driver function; it
 // is fetched once through the runtime so that the library needs no -lcuda.
+namespace {
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                    const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                    const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -86,9 +92,8 @@ EncodeTiledFn encodeTiled() {
   return fn;
 }
 
-// Tensor map of a column-major rows x cols FP32 matrix (leading dimension ld)
-// read in boxes of box_rows x box_cols; swizzle64 for k-contiguous tiles whose
-// rows are exactly 64 bytes.
+}  // namespace
+
 bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld, int box_rows,
                   int box_cols, bool swizzle64) {
   const EncodeTiledFn fn = encodeTiled();
@@ -107,17 +112,6 @@ bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------------------
-// Persistent schedule: one CTA per SM. Whole tiles are dealt round-robin;
-// when the tile count leaves a partial last wave, the last (full wave +
-// remainder) tiles are split by k iterations over all CTAs (stream-K), so every
-// SM finishes at the same time. Small problems with fewer tiles than SMs are
-// split the same way, down to kMinSkIters k slices per CTA.
-struct Schedule {
-  int grid = 0, dp_tiles = 0, sk_tiles = 0, sk_q = 0, sk_r = 0;
-};
-
-constexpr int kMinSkIters = 8;
-
 Schedule makeSchedule(long long tiles, int kiters, int sms) {
   Schedule s;
   const int t = static_cast<int>(tiles);
@@ -159,17 +153,7 @@ int smCount(int device) {
   return v;
 }
 
-constexpr size_t kSlotBytes = size_t{kern::kThreads} * kern::kSlotFloat4 * sizeof(float4);
-// Arrival counters: sk_tiles <= 2 * grid <= 2 * SMs, so 1024 counters cover
-// any GPU with up to 512 SMs.
-constexpr size_t kCounterRegionBytes = 4096;
-
-// Grow-only, stream-ordered workspace of the handle: [counters | slots].
-// Returns false (and the caller falls back to whole-tile scheduling) when it
-// cannot be provided.
-bool ensureWorkspace(sgblasContext *ctx, size_t counter_bytes, size_t slot_bytes, int device,
-                     cudaStream_t stream) {
-  const size_t need = counter_bytes + slot_bytes;
+bool ensureWorkspace(sgblasContext *ctx, size_t need, int device, cudaStream_t stream) {
   if (ctx->workspace != nullptr && ctx->workspace_device == device &&
       ctx->workspace_bytes >= need) {
     if (ctx->workspace_event != nullptr &&
@@ -206,97 +190,15 @@ bool ensureWorkspace(sgblasContext *ctx, size_t counter_bytes, size_t slot_bytes
   return true;
 }
 
-template <bool kTA, bool kTB, Beta kBeta, Src kSrc>
-sgblasStatus_t launchTiles(GemmParams p, sgblasContext *ctx, int device, cudaStream_t stream) {
-  using Plan = kern::Plan<kTA, kTB, kSrc>;
-  auto kernel = kern::sgemmKernel<kTA, kTB, kBeta, kSrc>;
-  static std::atomic<uint64_t> configured{0};
-  if (!configureKernel(reinterpret_cast<const void *>(kernel), device, kern::kSmemBytes,
-                       &configured))
-    return SGBLAS_STATUS_EXECUTION_FAILED;
-  p.tiles_m = (p.m + Plan::kBM - 1) / Plan::kBM;
-  p.tiles_n = (p.n + Plan::kBN - 1) / Plan::kBN;
-  p.group_m = 8;
-  p.kiters = (p.k + kern::kBK - 1) / kern::kBK;
-  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
-  if (tiles > INT_MAX / 2 || static_cast<long long>(p.kiters) * tiles > INT_MAX)
-    return SGBLAS_STATUS_NOT_SUPPORTED;
-  const int sms = smCount(device);
-  if (sms <= 0) return SGBLAS_STATUS_EXECUTION_FAILED;
-  Schedule s = makeSchedule(tiles, p.kiters, sms);
-  if (s.sk_tiles > 0) {
-    // The counter region has a fixed size so that the layout of the workspace
-    // is the same for every call: counters left at zero by one launch must not
-    // be overlapped by another launch's partial slots.
-    const size_t counter_bytes = kCounterRegionBytes;
-    if (static_cast<size_t>(s.sk_tiles) * sizeof(int) <= counter_bytes &&
-        ensureWorkspace(ctx, counter_bytes, 2 * static_cast<size_t>(s.grid) * kSlotBytes, device,
-                        stream)) {
-      p.counters = static_cast<int *>(ctx->workspace);
-      p.ws = reinterpret_cast<float4 *>(static_cast<char *>(ctx->workspace) + counter_bytes);
-    } else {  // no workspace: whole tiles only
-      s = Schedule{};
-      s.grid = static_cast<int>(std::min<long long>(tiles, sms));
-      s.dp_tiles = static_cast<int>(tiles);
-    }
-  }
-  p.grid = s.grid;
-  p.dp_tiles = s.dp_tiles;
-  p.sk_tiles = s.sk_tiles;
-  p.sk_q = s.sk_q;
-  p.sk_r = s.sk_r;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(s.grid));
-  cfg.blockDim = dim3(kern::kBlockThreads);
-  cfg.dynamicSmemBytes = kern::kSmemBytes;
-  cfg.stream = stream;
-  const sgblasStatus_t st = launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));
-  if (st == SGBLAS_STATUS_SUCCESS && s.sk_tiles > 0 &&
-      cudaEventRecord(static_cast<cudaEvent_t>(ctx->workspace_event), stream) != cudaSuccess) {
+bool markWorkspaceUse(sgblasContext *ctx, cudaStream_t stream) {
+  if (cudaEventRecord(static_cast<cudaEvent_t>(ctx->workspace_event), stream) != cudaSuccess) {
     (void)cudaGetLastError();
-    return SGBLAS_STATUS_EXECUTION_FAILED;
+    return false;
   }
-  return st;
+  return true;
 }
 
-template <bool kTA, bool kTB, Src kSrc>
-sgblasStatus_t launchByBeta(const GemmParams &p, sgblasContext *ctx, int device,
-                            cudaStream_t stream) {
-  if (p.beta == 0.0F) return launchTiles<kTA, kTB, Beta::kZero, kSrc>(p, ctx, device, stream);
-  if (p.beta == 1.0F) return launchTiles<kTA, kTB, Beta::kOne, kSrc>(p, ctx, device, stream);
-  return launchTiles<kTA, kTB, Beta::kGeneral, kSrc>(p, ctx, device, stream);
-}
-
-// TMA descriptors for the operand tiles the kernel stages: a [k][x] tile is a
-// box of (x extent) x BK elements of a x-contiguous matrix, a [x][k] tile a
-// BK x (x extent) box of a k-contiguous matrix with the 64B swizzle.
-template <bool kTA, bool kTB>
-bool encodeOperands(GemmParams &p) {
-  using Plan = kern::Plan<kTA, kTB, Src::kTma>;
-  const int a_ext = Plan::kPairIsA ? kern::kBP : kern::kBD;
-  const int b_ext = Plan::kPairIsA ? kern::kBD : kern::kBP;
-  const int a_rows = kTA ? p.k : p.m, a_cols = kTA ? p.m : p.k;
-  const int b_rows = kTB ? p.n : p.k, b_cols = kTB ? p.k : p.n;
-  const bool a_kx = Plan::kA == kern::Layout::kKX;
-  const bool b_kx = Plan::kB == kern::Layout::kKX;
-  return encodeMatrix(&p.tma_a, p.a, a_rows, a_cols, p.lda, a_kx ? kern::kBK : a_ext,
-                      a_kx ? a_ext : kern::kBK, a_kx) &&
-         encodeMatrix(&p.tma_b, p.b, b_rows, b_cols, p.ldb, b_kx ? kern::kBK : b_ext,
-                      b_kx ? b_ext : kern::kBK, b_kx);
-}
-
-template <bool kTA, bool kTB>
-sgblasStatus_t launchBySource(GemmParams &p, sgblasContext *ctx, int device, cudaStream_t stream) {
-  // TMA needs 16-byte aligned bases and leading dimensions that are a
-  // multiple of 16 bytes; TN has no [k][x] operand for TMA to deliver.
-  if constexpr (!(kTA && !kTB)) {
-    if (aligned16(p.a) && aligned16(p.b) && p.lda % 4 == 0 && p.ldb % 4 == 0 &&
-        encodeOperands<kTA, kTB>(p)) {
-      return launchByBeta<kTA, kTB, Src::kTma>(p, ctx, device, stream);
-    }
-  }
-  return launchByBeta<kTA, kTB, Src::kCopy>(p, ctx, device, stream);
-}
+namespace {
 
 sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOperation_t tb,
                              int m, int n, int k, float alpha, const float *a, int lda,
@@ -323,12 +225,14 @@ sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOpe
   p.alpha = alpha;
   p.beta = beta;
   p.err = err;
+  Scratch scratch;
+  scratch.ctx = ctx;
 
   const bool tA = ta == SGBLAS_OP_T, tB = tb == SGBLAS_OP_T;
-  if (!tA && !tB) return launchBySource<false, false>(p, ctx, device, stream);
-  if (!tA && tB) return launchBySource<false, true>(p, ctx, device, stream);
-  if (tA && !tB) return launchBySource<true, false>(p, ctx, device, stream);
-  return launchBySource<true, true>(p, ctx, device, stream);
+  if (!tA && !tB) return launchMode<false, false>(p, scratch, device, stream);
+  if (!tA && tB) return launchMode<false, true>(p, scratch, device, stream);
+  if (tA && !tB) return launchMode<true, false>(p, scratch, device, stream);
+  return launchMode<true, true>(p, scratch, device, stream);
 }
 
 }  // namespace

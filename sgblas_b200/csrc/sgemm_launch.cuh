@@ -1,0 +1,140 @@
+// Definition of launchMode<kTA, kTB> (declared in sgemm_launch.hpp); included
+// only by the per-mode translation units sgemm_mode_*.cu.
+#ifndef SGBLAS_B200_SGEMM_LAUNCH_CUH_
+#define SGBLAS_B200_SGEMM_LAUNCH_CUH_
+
+#include "device.hpp"
+#include "sgemm_launch.hpp"
+
+#include <algorithm>
+#include <atomic>
+#include <climits>
+#include <cstdint>
+
+namespace sgblas::detail {
+
+template <bool kTA, bool kTB, bool kPairIsA, kern::Beta kBeta, kern::Src kSrc>
+sgblasStatus_t launchTiles(kern::GemmParams p, const Scratch &scratch, int device,
+                           cudaStream_t stream) {
+  using Plan = kern::Plan<kTA, kTB, kPairIsA>;
+  auto kernel = kern::sgemmKernel<kTA, kTB, kPairIsA, kBeta, kSrc>;
+  static std::atomic<uint64_t> configured{0};
+  if (!configureKernel(reinterpret_cast<const void *>(kernel), device, kern::kSmemBytes,
+                       &configured))
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  p.tiles_m = (p.m + Plan::kBM - 1) / Plan::kBM;
+  p.tiles_n = (p.n + Plan::kBN - 1) / Plan::kBN;
+  p.group_m = 8;
+  p.kiters = (p.k + kern::kBK - 1) / kern::kBK;
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  if (tiles > INT_MAX / 2 || static_cast<long long>(p.kiters) * tiles > INT_MAX)
+    return SGBLAS_STATUS_NOT_SUPPORTED;
+  const int sms = smCount(device);
+  if (sms <= 0) return SGBLAS_STATUS_EXECUTION_FAILED;
+  Schedule s = makeSchedule(tiles, p.kiters, sms);
+  bool used_handle_workspace = false;
+  if (s.sk_tiles > 0) {
+    const size_t need = kCounterRegionBytes + 2 * static_cast<size_t>(s.grid) * kSlotBytes;
+    const bool counters_fit = static_cast<size_t>(s.sk_tiles) * sizeof(int) <= kCounterRegionBytes;
+    unsigned char *base = nullptr;
+    if (scratch.fixed != nullptr) {
+      // Fixed scratch: refuse rather than allocate. The counters are cleared
+      // in case an earlier launch did not finish.
+      if (!counters_fit || need > scratch.fixed_bytes) return SGBLAS_STATUS_NOT_SUPPORTED;
+      if (cudaMemsetAsync(scratch.fixed, 0, static_cast<size_t>(s.sk_tiles) * sizeof(int),
+                          stream) != cudaSuccess)
+        return launchStatus(cudaErrorUnknown);
+      base = scratch.fixed;
+    } else if (counters_fit && ensureWorkspace(scratch.ctx, need, device, stream)) {
+      base = static_cast<unsigned char *>(scratch.ctx->workspace);
+      used_handle_workspace = true;
+    }
+    if (base != nullptr) {
+      p.counters = reinterpret_cast<int *>(base);
+      p.ws = reinterpret_cast<float4 *>(base + kCounterRegionBytes);
+    } else {  // no workspace: whole tiles only
+      s = Schedule{};
+      s.grid = static_cast<int>(std::min<long long>(tiles, sms));
+      s.dp_tiles = static_cast<int>(tiles);
+    }
+  }
+  p.grid = s.grid;
+  p.dp_tiles = s.dp_tiles;
+  p.sk_tiles = s.sk_tiles;
+  p.sk_q = s.sk_q;
+  p.sk_r = s.sk_r;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(s.grid));
+  cfg.blockDim = dim3(kern::kBlockThreads);
+  cfg.dynamicSmemBytes = kern::kSmemBytes;
+  cfg.stream = stream;
+  const sgblasStatus_t st = launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));
+  if (st == SGBLAS_STATUS_SUCCESS && used_handle_workspace &&
+      !markWorkspaceUse(scratch.ctx, stream))
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  return st;
+}
+
+template <bool kTA, bool kTB, bool kPairIsA, kern::Src kSrc>
+sgblasStatus_t launchByBeta(const kern::GemmParams &p, const Scratch &scratch, int device,
+                            cudaStream_t stream) {
+  using kern::Beta;
+  if (p.beta == 0.0F)
+    return launchTiles<kTA, kTB, kPairIsA, Beta::kZero, kSrc>(p, scratch, device, stream);
+  if (p.beta == 1.0F)
+    return launchTiles<kTA, kTB, kPairIsA, Beta::kOne, kSrc>(p, scratch, device, stream);
+  return launchTiles<kTA, kTB, kPairIsA, Beta::kGeneral, kSrc>(p, scratch, device, stream);
+}
+
+// TMA when both bases are 16-byte aligned and both leading dimensions are a
+// multiple of 16 bytes (and the driver accepts the descriptors); otherwise
+// cp.async, per operand in the widest size (16, 8 or 4 bytes) its base and
+// leading dimension allow. Each operand is staged in its natural layout.
+template <bool kTA, bool kTB, bool kPairIsA>
+sgblasStatus_t launchOriented(kern::GemmParams p, const Scratch &scratch, int device,
+                              cudaStream_t stream) {
+  using Plan = kern::Plan<kTA, kTB, kPairIsA>;
+  using kern::Layout;
+  if (aligned16(p.a) && aligned16(p.b) && p.lda % 4 == 0 && p.ldb % 4 == 0) {
+    const bool a_kx = Plan::kA == Layout::kKX;
+    const bool b_kx = Plan::kB == Layout::kKX;
+    const int bk = kern::kBK;
+    if (encodeMatrix(&p.tma_a, p.a, kTA ? p.k : p.m, kTA ? p.m : p.k, p.lda,
+                     a_kx ? bk : Plan::kAExt, a_kx ? Plan::kAExt : bk, a_kx) &&
+        encodeMatrix(&p.tma_b, p.b, kTB ? p.n : p.k, kTB ? p.k : p.n, p.ldb,
+                     b_kx ? bk : Plan::kBExt, b_kx ? Plan::kBExt : bk, b_kx))
+      return launchByBeta<kTA, kTB, kPairIsA, kern::Src::kTma>(p, scratch, device, stream);
+  }
+  // Widest cp.async the operand's alignment allows.
+  auto vec = [](const float *ptr, int ld) {
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(ptr);
+    if (addr % 16 == 0 && ld % 4 == 0) return 4;
+    if (addr % 8 == 0 && ld % 2 == 0) return 2;
+    return 1;
+  };
+  p.a_vec = vec(p.a, p.lda);
+  p.b_vec = vec(p.b, p.ldb);
+  return launchByBeta<kTA, kTB, kPairIsA, kern::Src::kCopy>(p, scratch, device, stream);
+}
+
+// Orientation: the pair operand spans 256 rows of its side of C, the broadcast
+// operand 128. Choose the orientation with less padded tile area, then the one
+// that transposes fewer elements per k step.
+template <bool kTA, bool kTB>
+sgblasStatus_t launchMode(kern::GemmParams p, const Scratch &scratch, int device,
+                          cudaStream_t stream) {
+  using PA = kern::Plan<kTA, kTB, true>;
+  using PB = kern::Plan<kTA, kTB, false>;
+  auto padded = [](long long x, long long t) { return (x + t - 1) / t * t; };
+  const long long area_a = padded(p.m, PA::kBM) * padded(p.n, PA::kBN);
+  const long long area_b = padded(p.m, PB::kBM) * padded(p.n, PB::kBN);
+  constexpr int trans_a = (PA::kTransP ? kern::kBP : 0) + (PA::kTransD ? kern::kBD : 0);
+  constexpr int trans_b = (PB::kTransP ? kern::kBP : 0) + (PB::kTransD ? kern::kBD : 0);
+  const bool pair_is_a = area_a < area_b || (area_a == area_b && trans_a <= trans_b);
+  if (pair_is_a) return launchOriented<kTA, kTB, true>(p, scratch, device, stream);
+  return launchOriented<kTA, kTB, false>(p, scratch, device, stream);
+}
+
+}  // namespace sgblas::detail
+
+#endif  // SGBLAS_B200_SGEMM_LAUNCH_CUH_

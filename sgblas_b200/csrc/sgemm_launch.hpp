@@ -1,0 +1,82 @@
+// Host-side launch of the tile kernel: schedule, operand orientation, staging
+// path and stream-K scratch. Shared by sgblasSgemm (sgemm.cu), which takes
+// its scratch from the handle's workspace, and sgblasSgemmNoAlloc
+// (sgemm_noalloc.cu), which uses a fixed array. The per-mode templates are
+// instantiated in sgemm_mode_{nn,nt,tn,tt}.cu so that they compile in
+// parallel.
+#ifndef SGBLAS_B200_SGEMM_LAUNCH_HPP_
+#define SGBLAS_B200_SGEMM_LAUNCH_HPP_
+
+#include "context.hpp"
+#include "sgemm_tile.cuh"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+
+namespace sgblas::detail {
+
+sgblasStatus_t launchStatus(cudaError_t e);
+
+// Tensor map of a column-major rows x cols FP32 matrix (leading dimension ld)
+// read in boxes of box_rows x box_cols; swizzle64 for k-contiguous tiles whose
+// rows are exactly 64 bytes. False if the driver refuses it.
+bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld, int box_rows,
+                  int box_cols, bool swizzle64);
+
+bool aligned16(const void *p);
+
+int smCount(int device);
+
+// Persistent schedule: one CTA per SM. Whole tiles are dealt round-robin;
+// when the tile count leaves a partial last wave, the last (full wave +
+// remainder) tiles are split by k iterations over all CTAs (stream-K), so every
+// SM finishes at the same time. Small problems with fewer tiles than SMs are
+// split the same way, down to kMinSkIters k slices per CTA.
+struct Schedule {
+  int grid = 0, dp_tiles = 0, sk_tiles = 0, sk_q = 0, sk_r = 0;
+};
+constexpr int kMinSkIters = 8;
+Schedule makeSchedule(long long tiles, int kiters, int sms);
+
+// Scratch layout: [arrival counters (kCounterRegionBytes) | partial slots].
+// sk_tiles <= 2 * grid <= 2 * SMs, so 1024 counters cover any GPU with up to
+// 512 SMs; the counter region has a fixed size so that the layout is the same
+// for every call (counters left at zero by one launch must never be
+// overlapped by another launch's slots).
+constexpr size_t kSlotBytes = size_t{kern::kThreads} * kern::kSlotFloat4 * sizeof(float4);
+constexpr size_t kCounterRegionBytes = 4096;
+
+// Where a launch takes its stream-K scratch from.
+struct Scratch {
+  sgblasContext *ctx = nullptr;      // the handle's workspace (may allocate), or
+  unsigned char *fixed = nullptr;    // a fixed device array of fixed_bytes
+  size_t fixed_bytes = 0;
+};
+
+// Provides [counters | 2*grid slots] for a stream-K launch on `stream`.
+// The handle workspace is grow-only and allocated stream-ordered; false when
+// it cannot be provided (the caller then schedules whole tiles only).
+bool ensureWorkspace(sgblasContext *ctx, size_t bytes, int device, cudaStream_t stream);
+// Marks the end of a launch that used the handle workspace.
+bool markWorkspaceUse(sgblasContext *ctx, cudaStream_t stream);
+
+// Launches one product of transpose mode (kTA, kTB). p carries the problem
+// (pointers, sizes, alpha, beta, error word); the launcher fills in the rest.
+template <bool kTA, bool kTB>
+sgblasStatus_t launchMode(kern::GemmParams p, const Scratch &scratch, int device,
+                          cudaStream_t stream);
+
+extern template sgblasStatus_t launchMode<false, false>(kern::GemmParams, const Scratch &, int,
+                                                        cudaStream_t);
+extern template sgblasStatus_t launchMode<false, true>(kern::GemmParams, const Scratch &, int,
+                                                       cudaStream_t);
+extern template sgblasStatus_t launchMode<true, false>(kern::GemmParams, const Scratch &, int,
+                                                       cudaStream_t);
+extern template sgblasStatus_t launchMode<true, true>(kern::GemmParams, const Scratch &, int,
+                                                      cudaStream_t);
+
+}  // namespace sgblas::detail
+
+#endif  // SGBLAS_B200_SGEMM_LAUNCH_HPP_

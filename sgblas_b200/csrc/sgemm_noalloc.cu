@@ -25,31 +25,24 @@
 // the same persistent tile kernel sgblasSgemm launches (sgemm_tile.cuh).
 #include "context.hpp"
 #include "device.hpp"
-#include "sgemm_tile.cuh"
+#include "sgemm_launch.hpp"
 #include "validation.hpp"
 
 #include <sgblas/sgblas_ext.h>
 
-#include <cuda.h>
 #include <cuda_runtime.h>
 
-#include <algorithm>
 #include <atomic>
-#include <climits>
-#include <cstdint>
 
 namespace {
 
-using sgblas::kern::Beta;
-using sgblas::kern::GemmParams;
-using sgblas::kern::Src;
-
-// Scratch layout: [arrival counters | partial-tile slots]. 38 MiB holds the
-// counters of up to 1024 split tiles and two 128 KiB partial slots for each of
-// up to 151 persistent CTAs (one per SM).
-constexpr size_t kCounterBytes = 4096;
-constexpr size_t kSlotBytes = size_t{sgblas::kern::kThreads} * sgblas::kern::kSlotFloat4 * sizeof(float4);
+// Scratch layout (sgemm_launch.hpp): [arrival counters | partial-tile slots].
+// 38 MiB holds the 4 KiB counter region and two 128 KiB partial slots for each
+// of up to 151 persistent CTAs (one per SM).
 constexpr size_t kScratchBytes = size_t{38} << 20;
+static_assert(sgblas::detail::kCounterRegionBytes + 2 * 151 * sgblas::detail::kSlotBytes <=
+                  kScratchBytes,
+              "scratch sized for 151 SMs");
 
 }  // namespace
 
@@ -72,143 +65,6 @@ unsigned char *scratchAddress(int device) {
   }
   g_scratch_address[device].store(ptr, std::memory_order_release);
   return ptr;
-}
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encodeTiled() {
-  static const EncodeTiledFn fn = [] {
-    void *f = nullptr;
-    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault,
-                                         &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess) {
-      (void)cudaGetLastError();
-      return static_cast<EncodeTiledFn>(nullptr);
-    }
-    return reinterpret_cast<EncodeTiledFn>(f);
-  }();
-  return fn;
-}
-
-bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld, int box_rows,
-                  int box_cols, bool swizzle64) {
-  const EncodeTiledFn fn = encodeTiled();
-  if (fn == nullptr) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(cols)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * sizeof(float)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_rows), static_cast<cuuint32_t>(box_cols)};
-  const cuuint32_t elem_strides[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides, box,
-            elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            swizzle64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-sgblasStatus_t launchStatus(cudaError_t e) {
-  if (e == cudaSuccess) return SGBLAS_STATUS_SUCCESS;
-  (void)cudaGetLastError();
-  return SGBLAS_STATUS_EXECUTION_FAILED;
-}
-
-// The same persistent schedule sgblasSgemm uses (whole tiles, then stream-K
-// for a partial last wave or for problems with fewer tiles than SMs).
-constexpr int kMinSkIters = 8;
-
-template <bool kTA, bool kTB, Beta kBeta, Src kSrc>
-sgblasStatus_t launch(GemmParams p, int device, cudaStream_t stream) {
-  using Plan = sgblas::kern::Plan<kTA, kTB, kSrc>;
-  auto kernel = sgblas::kern::sgemmKernel<kTA, kTB, kBeta, kSrc>;
-  static std::atomic<uint64_t> configured{0};
-  if (!sgblas::detail::configureKernel(reinterpret_cast<const void *>(kernel), device,
-                                       sgblas::kern::kSmemBytes, &configured))
-    return SGBLAS_STATUS_EXECUTION_FAILED;
-  p.tiles_m = (p.m + Plan::kBM - 1) / Plan::kBM;
-  p.tiles_n = (p.n + Plan::kBN - 1) / Plan::kBN;
-  p.group_m = 8;
-  p.kiters = (p.k + sgblas::kern::kBK - 1) / sgblas::kern::kBK;
-  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
-  if (tiles > INT_MAX / 2 || static_cast<long long>(p.kiters) * tiles > INT_MAX)
-    return SGBLAS_STATUS_NOT_SUPPORTED;
-  int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) {
-    (void)cudaGetLastError();
-    return SGBLAS_STATUS_EXECUTION_FAILED;
-  }
-  const int t = static_cast<int>(tiles);
-  p.dp_tiles = p.sk_tiles = p.sk_q = p.sk_r = 0;
-  if (t >= sms) {
-    p.grid = sms;
-    const int waves = t / sms, rem = t % sms;
-    if (rem == 0 || p.kiters < 2 * kMinSkIters) {
-      p.dp_tiles = t;
-    } else {
-      p.dp_tiles = (waves - 1) * sms;
-      p.sk_tiles = t - p.dp_tiles;
-    }
-  } else {
-    p.grid = static_cast<int>(std::min<long long>(
-        sms, std::max<long long>(tiles, tiles * p.kiters / kMinSkIters)));
-    if (p.grid == t) p.dp_tiles = t;
-    else p.sk_tiles = t;
-  }
-  if (p.sk_tiles > 0) {
-    const long long it = static_cast<long long>(p.sk_tiles) * p.kiters;
-    p.sk_q = static_cast<int>(it / p.grid);
-    p.sk_r = static_cast<int>(it % p.grid);
-    // The fixed scratch must hold this schedule: refuse rather than allocate.
-    if (static_cast<size_t>(p.sk_tiles) * sizeof(int) > kCounterBytes ||
-        kCounterBytes + 2 * static_cast<size_t>(p.grid) * kSlotBytes > kScratchBytes)
-      return SGBLAS_STATUS_NOT_SUPPORTED;
-    unsigned char *scratch = scratchAddress(device);
-    if (scratch == nullptr) return SGBLAS_STATUS_EXECUTION_FAILED;
-    // The counters must start at zero; a previous call normally leaves them
-    // so, but one that did not finish might not have.
-    if (cudaMemsetAsync(scratch, 0, static_cast<size_t>(p.sk_tiles) * sizeof(int), stream) !=
-        cudaSuccess)
-      return launchStatus(cudaErrorUnknown);
-    p.counters = reinterpret_cast<int *>(scratch);
-    p.ws = reinterpret_cast<float4 *>(scratch + kCounterBytes);
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(p.grid));
-  cfg.blockDim = dim3(sgblas::kern::kBlockThreads);
-  cfg.dynamicSmemBytes = sgblas::kern::kSmemBytes;
-  cfg.stream = stream;
-  return launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));
-}
-
-template <bool kTA, bool kTB, Src kSrc>
-sgblasStatus_t launchByBeta(const GemmParams &p, int device, cudaStream_t stream) {
-  if (p.beta == 0.0F) return launch<kTA, kTB, Beta::kZero, kSrc>(p, device, stream);
-  if (p.beta == 1.0F) return launch<kTA, kTB, Beta::kOne, kSrc>(p, device, stream);
-  return launch<kTA, kTB, Beta::kGeneral, kSrc>(p, device, stream);
-}
-
-bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-template <bool kTA, bool kTB>
-sgblasStatus_t launchBySource(GemmParams &p, int device, cudaStream_t stream) {
-  if constexpr (!(kTA && !kTB)) {
-    using Plan = sgblas::kern::Plan<kTA, kTB, Src::kTma>;
-    if (aligned16(p.a) && aligned16(p.b) && p.lda % 4 == 0 && p.ldb % 4 == 0) {
-      const int a_ext = Plan::kPairIsA ? sgblas::kern::kBP : sgblas::kern::kBD;
-      const int b_ext = Plan::kPairIsA ? sgblas::kern::kBD : sgblas::kern::kBP;
-      const bool a_kx = Plan::kA == sgblas::kern::Layout::kKX;
-      const bool b_kx = Plan::kB == sgblas::kern::Layout::kKX;
-      const int bk = sgblas::kern::kBK;
-      if (encodeMatrix(&p.tma_a, p.a, kTA ? p.k : p.m, kTA ? p.m : p.k, p.lda,
-                       a_kx ? bk : a_ext, a_kx ? a_ext : bk, a_kx) &&
-          encodeMatrix(&p.tma_b, p.b, kTB ? p.n : p.k, kTB ? p.k : p.n, p.ldb,
-                       b_kx ? bk : b_ext, b_kx ? b_ext : bk, b_kx))
-        return launchByBeta<kTA, kTB, Src::kTma>(p, device, stream);
-    }
-  }
-  return launchByBeta<kTA, kTB, Src::kCopy>(p, device, stream);
 }
 
 }  // namespace
@@ -237,7 +93,9 @@ extern "C" sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperat
   }
   unsigned *err = deviceErrorWord(device);
   if (err == nullptr) return SGBLAS_STATUS_EXECUTION_FAILED;
-  GemmParams p = {};
+  unsigned char *scratch = scratchAddress(device);
+  if (scratch == nullptr) return SGBLAS_STATUS_EXECUTION_FAILED;
+  sgblas::kern::GemmParams p = {};
   p.a = a;
   p.b = b;
   p.c = c;
@@ -251,9 +109,12 @@ extern "C" sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperat
   p.beta = plan.beta;
   p.err = err;
   const auto stream = static_cast<cudaStream_t>(handle->stream);
+  Scratch fixed;
+  fixed.fixed = scratch;
+  fixed.fixed_bytes = kScratchBytes;
   const bool tA = transa == SGBLAS_OP_T, tB = transb == SGBLAS_OP_T;
-  if (!tA && !tB) return launchBySource<false, false>(p, device, stream);
-  if (!tA && tB) return launchBySource<false, true>(p, device, stream);
-  if (tA && !tB) return launchBySource<true, false>(p, device, stream);
-  return launchBySource<true, true>(p, device, stream);
+  if (!tA && !tB) return launchMode<false, false>(p, fixed, device, stream);
+  if (!tA && tB) return launchMode<false, true>(p, fixed, device, stream);
+  if (tA && !tB) return launchMode<true, false>(p, fixed, device, stream);
+  return launchMode<true, true>(p, fixed, device, stream);
 }

@@ -14,14 +14,18 @@
 // Operand roles. FFMA2 multiplies a register pair by a register pair. The
 // "pair" operand P feeds two elements adjacent along its free dimension (half
 // of a 16-byte shared-memory load); the "broadcast" operand D feeds one element
-// to both lanes. P must sit in shared memory as [k][x] (x contiguous); D may be
-// [k][x] or [x][k].
+// to both lanes. Either A or B can be P (a template parameter): the
+// orientation with the smaller padded tile area is chosen per call.
 //
-// Shared-memory tile layouts (a pipeline stage holds one P and one D tile):
+// Shared-memory tile layouts:
 //   kXK : [BK][BX] floats, x contiguous -- what TMA writes when x is the
-//         contiguous global dimension.
+//         contiguous global dimension (A not transposed, B transposed).
 //   kKX : [BX][BK] floats, k contiguous, 64-byte rows with the TMA 64B swizzle
 //         (16-byte chunk index ^= (row >> 1) & 3).
+// Operands are staged in their natural layout; the compute warps read both P
+// and D as [k][x] (reads from [x][k] rows measured ~10% slower in the inner
+// loop), so the producer warpgroup transposes every [x][k]-staged operand into
+// a [k][x] buffer a few iterations ahead of its use.
 //
 // CTA: three warpgroups, one CTA per SM.
 //   - Warpgroups 0-1 (256 threads, 8 warps) compute a 256 (P) x 128 (D) tile;
@@ -29,11 +33,11 @@
 //     4+2 shared loads). Warps form 2 (P) x 4 (D); lane bits lp = lane % 8,
 //     ld = lane / 8.
 //       P coordinates: 128*wp + 4*lp + {0..3} + 32*q, q = 0..3.
-//       D coordinates ([k][x] tile): 32*wd + 4*ld + {0..3} + {0, 16}.
+//       D coordinates: 32*wd + 4*ld + {0..3} + {0, 16}.
 //   - Warpgroup 2 (128 threads) is the producer: one thread issues the TMA
 //     tile loads (or all 128 issue cp.async copies), and all 128 transpose
-//     [x][k] broadcast tiles into [k][x] buffers. It gives registers to the
-//     compute warpgroups (setmaxnreg), so that those keep 232.
+//     [x][k] tiles into [k][x] buffers. It gives registers to the compute
+//     warpgroups (setmaxnreg), so that those keep 232.
 //   Producer and consumers meet only at mbarriers (stage full/empty,
 //   transposed buffer full/empty), so no warp ever waits on a CTA-wide
 //   barrier inside the main loop.
@@ -51,7 +55,7 @@ constexpr int kBP = 256;   // pair-operand tile extent
 constexpr int kBD = 128;   // broadcast-operand tile extent
 constexpr int kBK = 16;    // k slice per pipeline stage
 constexpr int kStages = 6;
-constexpr int kTransBufs = 3;   // ring of transposed [k][x] broadcast tiles
+constexpr int kTransBufs = 3;   // ring of transposed [k][x] tiles
 constexpr int kTP = 16;         // pair-operand elements per thread
 constexpr int kTD = 8;          // broadcast-operand elements per thread
 constexpr int kWarpsP = kBP / (8 * kTP);   // warps along P (8 lanes x kTP each)
@@ -75,10 +79,11 @@ constexpr int kDupFloats = kBD * kBK;
 constexpr int kPairBytes = kPairFloats * 4;   // 16 KiB
 constexpr int kDupBytes = kDupFloats * 4;     // 8 KiB
 constexpr int kStageBytes = kPairBytes + kDupBytes;
-constexpr int kTransBytes = kTransBufs * kDupBytes;
+constexpr int kTransBytes = kTransBufs * kStageBytes;  // room for both operands
 constexpr int kBarrierBytes = 8 * (2 * kStages + 2 * kTransBufs);
 constexpr int kSmemAlign = 1024;
 constexpr int kSmemBytes = kStages * kStageBytes + kTransBytes + kBarrierBytes + kSmemAlign;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 
 enum class Beta { kZero, kOne, kGeneral };
 enum class Src { kTma, kCopy };
@@ -107,13 +112,15 @@ struct GemmParams {
   int sk_q, sk_r;
   float4 *ws;         // 2 * grid partial-tile slots of kThreads * kSlotFloat4 float4
   int *counters;      // sk_tiles arrival counters, zero between launches
+  // cp.async path: floats per copy (1, 2 or 4) allowed by each operand's base
+  // alignment and leading dimension.
+  int a_vec, b_vec;
 };
 
 // One unit of a CTA's work: k iterations [kb, ke) of tile `tile`.
 struct Item {
   int tile, kb, ke;
 };
-
 
 __device__ __forceinline__ int skBegin(const GemmParams &p, int c) {
   return c * p.sk_q + min(c, p.sk_r);
@@ -158,22 +165,22 @@ __device__ __forceinline__ uint32_t kxOffset(int x, int k) {
   return static_cast<uint32_t>(x * 64 + ((((k >> 2) ^ (x >> 1)) & 3) << 4) + ((k & 3) << 2));
 }
 
-// Which operand plays which role, and the tile shape that follows.
-template <bool kTA, bool kTB, Src kSrc>
+// Operand roles, staged layouts and the tile shape that follows.
+template <bool kTA, bool kTB, bool kPairIsA_>
 struct Plan {
-  // Shared-memory layout of each operand. The cp.async path may transpose A
-  // while staging it, so it always stages A as [k][m].
-  static constexpr Layout kA = (kSrc == Src::kTma && kTA) ? Layout::kKX : Layout::kXK;
+  static constexpr bool kPairIsA = kPairIsA_;
+  // Natural staged layout: [k][x] when x is the contiguous global dimension.
+  static constexpr Layout kA = kTA ? Layout::kKX : Layout::kXK;
   static constexpr Layout kB = kTB ? Layout::kXK : Layout::kKX;
-  static constexpr bool kPairIsA = (kA == Layout::kXK);
+  static constexpr int kAExt = kPairIsA ? kBP : kBD;  // tile extent along m
+  static constexpr int kBExt = kPairIsA ? kBD : kBP;  // tile extent along n
+  static constexpr Layout kP = kPairIsA ? kA : kB;
   static constexpr Layout kD = kPairIsA ? kB : kA;
-  static_assert(kPairIsA || kB == Layout::kXK, "one operand must be staged as [k][x]");
-  // A broadcast tile staged as [x][k] is transposed into [k][x] before use:
-  // broadcast reads from [x][k] rows measured ~10% slower in the inner loop.
+  static constexpr bool kTransP = (kP == Layout::kKX);
   static constexpr bool kTransD = (kD == Layout::kKX);
-  static constexpr Layout kCompD = Layout::kXK;
-  static constexpr int kBM = kPairIsA ? kBP : kBD;
-  static constexpr int kBN = kPairIsA ? kBD : kBP;
+  static constexpr bool kTrans = kTransP || kTransD;
+  static constexpr int kBM = kAExt;
+  static constexpr int kBN = kBExt;
 };
 
 // Tile index -> (tile_m, tile_n): groups of group_m tile rows are walked
@@ -189,94 +196,83 @@ __device__ __forceinline__ void rasterTile(const GemmParams &p, int t, int *tm, 
 }
 
 // ---- cp.async staging (any alignment, any leading dimension, tails) --------
-// Writes the layouts the kernel reads: A as [k][m] (P, kBP wide), B as [k][n]
-// or swizzled [n][k] (D, kBD wide), zero-filled outside the matrix. Global
-// reads are coalesced along each operand's contiguous dimension.
-template <bool kTA, bool kTB>
-__device__ __forceinline__ void copyTile(const GemmParams &p, float *sa, float *sb, int m0, int n0,
-                                         int k0, int tid) {
+// One operand tile in its natural layout (the layout TMA would write), by the
+// producer warpgroup, in copies of kVec floats along the contiguous dimension
+// (4 or 8 bytes when the operand's alignment forbids 16), zero-filled outside
+// the matrix: a copy that straddles the matrix edge reads only its in-range
+// floats. Global reads are coalesced along the contiguous dimension. Element
+// (x, k) of the stored matrix is src[x + k*ld] for an [k][x] tile and
+// src[k + x*ld] for an [x][k] tile; x0/k0 are the tile origin, x_limit/k_limit
+// the matrix extents. Requires src and ld to be multiples of kVec floats.
+template <int kExt, bool kKx, int kVec>
+__device__ __forceinline__ void copyOperandVec(const float *src, int ld, int x_limit, int k_limit,
+                                               float *dst, int x0, int k0, int tid) {
   constexpr int kN = kProducerThreads;
+  constexpr int kRun = kKx ? kBK / kVec : kExt / kVec;  // copies along the contiguous dim
 #pragma unroll 4
-  for (int r = 0; r < kPairFloats / kN; ++r) {
+  for (int r = 0; r < kExt * kBK / (kVec * kN); ++r) {
     const int e = tid + r * kN;
-    const int mm = kTA ? e / kBK : e % kBP;
-    const int kk = kTA ? e % kBK : e / kBP;
-    const int gm = m0 + mm, gk = k0 + kk;
-    const bool ok = gm < p.m && gk < p.k;
-    const float *src = p.a;
-    if (ok) {
-      src = kTA ? p.a + static_cast<size_t>(gk) + static_cast<size_t>(gm) * p.lda
-                : p.a + static_cast<size_t>(gm) + static_cast<size_t>(gk) * p.lda;
+    const int x = kKx ? e / kRun : (e % kRun) * kVec;
+    const int kk = kKx ? (e % kRun) * kVec : e / kRun;
+    const int gx = x0 + x, gk = k0 + kk;
+    int valid;
+    if constexpr (kKx) valid = gx < x_limit ? min(max(k_limit - gk, 0), kVec) : 0;
+    else valid = gk < k_limit ? min(max(x_limit - gx, 0), kVec) : 0;
+    const float *s = src;
+    if (valid > 0) {
+      s = kKx ? src + static_cast<size_t>(gk) + static_cast<size_t>(gx) * ld
+              : src + static_cast<size_t>(gx) + static_cast<size_t>(gk) * ld;
     }
-    cpAsync4(sa + kk * kBP + mm, src, ok ? 4u : 0u);
-  }
-#pragma unroll 4
-  for (int r = 0; r < kDupFloats / kN; ++r) {
-    const int e = tid + r * kN;
-    const int nn = kTB ? e % kBD : e / kBK;
-    const int kk = kTB ? e / kBD : e % kBK;
-    const int gn = n0 + nn, gk = k0 + kk;
-    const bool ok = gn < p.n && gk < p.k;
-    const float *src = p.b;
-    if (ok) {
-      src = kTB ? p.b + static_cast<size_t>(gn) + static_cast<size_t>(gk) * p.ldb
-                : p.b + static_cast<size_t>(gk) + static_cast<size_t>(gn) * p.ldb;
-    }
-    float *dst = kTB ? sb + kk * kBD + nn
-                     : reinterpret_cast<float *>(reinterpret_cast<char *>(sb) + kxOffset(nn, kk));
-    cpAsync4(dst, src, ok ? 4u : 0u);
+    float *d = kKx ? reinterpret_cast<float *>(reinterpret_cast<char *>(dst) + kxOffset(x, kk))
+                   : dst + kk * kExt + x;
+    cpAsyncN<4 * kVec>(d, s, static_cast<uint32_t>(4 * valid));
   }
 }
 
-// Per-thread addressing of the broadcast tile.
-struct DupAddr {
-  uint32_t base;        // kXK: float index of the first column; kKX: byte offset of row 0
-  uint32_t chunk[4];    // kKX: swizzled byte offset of each 16-byte k chunk
-};
+template <int kExt, bool kKx>
+__device__ __forceinline__ void copyOperand(const float *src, int ld, int x_limit, int k_limit,
+                                            float *dst, int x0, int k0, int tid, int vec) {
+  if (vec == 4) copyOperandVec<kExt, kKx, 4>(src, ld, x_limit, k_limit, dst, x0, k0, tid);
+  else if (vec == 2) copyOperandVec<kExt, kKx, 2>(src, ld, x_limit, k_limit, dst, x0, k0, tid);
+  else copyOperandVec<kExt, kKx, 1>(src, ld, x_limit, k_limit, dst, x0, k0, tid);
+}
 
-// [x][k] broadcast tile (64-byte swizzled rows) -> [k][x] (kBD floats per k),
-// by the producer warpgroup: thread t moves row t. A warp reads 32
+// [x][k] tile of kRows rows (64-byte swizzled) -> [k][x] (kRows floats per k),
+// by the producer warpgroup: thread t moves rows t, t+128, ... A warp reads 32
 // consecutive rows at one chunk -- conflict-free thanks to the swizzle -- and
 // writes 32 consecutive floats per k.
-__device__ __forceinline__ void transposeDup(const float *src, float *dst, int tid) {
-  static_assert(kProducerThreads == kBD && kBK == 16, "one row per producer thread");
-  const char *row = reinterpret_cast<const char *>(src) + tid * 64;
-  const int phase = (tid >> 1) & 3;
-  float *d = dst + tid;
+template <int kRows>
+__device__ __forceinline__ void transposeKX(const float *src, float *dst, int tid) {
+  static_assert(kRows % kProducerThreads == 0 && kBK == 16, "row split");
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const float4 v = *reinterpret_cast<const float4 *>(row + ((c ^ phase) << 4));
-    d[(4 * c + 0) * kBD] = v.x;
-    d[(4 * c + 1) * kBD] = v.y;
-    d[(4 * c + 2) * kBD] = v.z;
-    d[(4 * c + 3) * kBD] = v.w;
+  for (int r = tid; r < kRows; r += kProducerThreads) {
+    const char *row = reinterpret_cast<const char *>(src) + r * 64;
+    const int phase = (r >> 1) & 3;
+    float *d = dst + r;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float4 v = *reinterpret_cast<const float4 *>(row + ((c ^ phase) << 4));
+      d[(4 * c + 0) * kRows] = v.x;
+      d[(4 * c + 1) * kRows] = v.y;
+      d[(4 * c + 2) * kRows] = v.z;
+      d[(4 * c + 3) * kRows] = v.w;
+    }
   }
 }
 
 // ---- the FFMA2 micro-kernel over one BK slice ------------------------------
-template <Layout kD>
+// sp: [k][kBP] pair tile, sd: [k][kBD] broadcast tile.
 __device__ __forceinline__ void computeStage(const float *sp, const float *sd, int p_base,
-                                             const DupAddr &da, float2 (&acc)[kTP / 2][kTD]) {
+                                             int d_base, float2 (&acc)[kTP / 2][kTD]) {
 #pragma unroll
   for (int k = 0; k < kBK; k += 2) {
     float dv[2][kTD];
-    if constexpr (kD == Layout::kXK) {
 #pragma unroll
-      for (int kk = 0; kk < 2; ++kk) {
-        const float4 d0 = *reinterpret_cast<const float4 *>(sd + (k + kk) * kBD + da.base);
-        const float4 d1 = *reinterpret_cast<const float4 *>(sd + (k + kk) * kBD + da.base + 16);
-        dv[kk][0] = d0.x; dv[kk][1] = d0.y; dv[kk][2] = d0.z; dv[kk][3] = d0.w;
-        dv[kk][4] = d1.x; dv[kk][5] = d1.y; dv[kk][6] = d1.z; dv[kk][7] = d1.w;
-      }
-    } else {
-      const char *row0 = reinterpret_cast<const char *>(sd) + da.base + da.chunk[k >> 2] +
-                         ((k & 3) << 2);
-#pragma unroll
-      for (int j = 0; j < kTD; ++j) {
-        const float2 v = *reinterpret_cast<const float2 *>(row0 + 512 * j);
-        dv[0][j] = v.x;
-        dv[1][j] = v.y;
-      }
+    for (int kk = 0; kk < 2; ++kk) {
+      const float4 d0 = *reinterpret_cast<const float4 *>(sd + (k + kk) * kBD + d_base);
+      const float4 d1 = *reinterpret_cast<const float4 *>(sd + (k + kk) * kBD + d_base + 16);
+      dv[kk][0] = d0.x; dv[kk][1] = d0.y; dv[kk][2] = d0.z; dv[kk][3] = d0.w;
+      dv[kk][4] = d1.x; dv[kk][5] = d1.y; dv[kk][6] = d1.z; dv[kk][7] = d1.w;
     }
 #pragma unroll
     for (int kk = 0; kk < 2; ++kk) {
@@ -322,16 +318,16 @@ __device__ __forceinline__ float epilogueValue(float acc, float alpha, float bet
 //
 // Synchronisation (all mbarriers, all waits bounded):
 //   full[s]     stage s holds iteration i's tiles   (TMA bytes / cp.async)
-//   empty[s]    the 8 compute warps are done with stage s's pair tile
-//   tfull[t]    transposed broadcast buffer t is written (128 producer threads)
+//   empty[s]    the 8 compute warps are done with stage s
+//   tfull[t]    transposed buffer t is written (128 producer threads)
 //   tempty[t]   the 8 compute warps are done with buffer t
 // A wait that times out raises the device error flag; from then on that
 // thread skips its waits (results are garbage and flagged) but still runs
 // every loop to its end, so that no thread is left behind at a barrier.
-template <bool kTA, bool kTB, Beta kBeta, Src kSrc>
+template <bool kTA, bool kTB, bool kPairIsA, Beta kBeta, Src kSrc>
 __global__ void __launch_bounds__(kBlockThreads, 1)
     sgemmKernel(const __grid_constant__ GemmParams p) {
-  using P = Plan<kTA, kTB, kSrc>;
+  using P = Plan<kTA, kTB, kPairIsA>;
   extern __shared__ unsigned char smem_raw[];
   __shared__ int last_arrival;
   // Align within the shared window by offsetting smem_raw itself: pointers
@@ -344,13 +340,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   uint64_t *empty = full + kStages;
   uint64_t *tfull = empty + kStages;
   uint64_t *tempty = tfull + kTransBufs;
-  auto tbuf = [&](int i) {
-    return reinterpret_cast<float *>(smem + kStages * kStageBytes + i * kDupBytes);
-  };
-  // Stage s: the pair tile at offset 0, the broadcast tile after it.
+  // Stage s: the pair tile at offset 0, the broadcast tile after it; the
+  // transposed buffers use the same split.
   auto stageP = [&](int s) { return reinterpret_cast<float *>(smem + s * kStageBytes); };
   auto stageD = [&](int s) {
     return reinterpret_cast<float *>(smem + s * kStageBytes + kPairBytes);
+  };
+  auto tbufP = [&](int t) {
+    return reinterpret_cast<float *>(smem + kStages * kStageBytes + t * kStageBytes);
+  };
+  auto tbufD = [&](int t) {
+    return reinterpret_cast<float *>(smem + kStages * kStageBytes + t * kStageBytes + kPairBytes);
   };
   auto stageA = [&](int s) { return P::kPairIsA ? stageP(s) : stageD(s); };
   auto stageB = [&](int s) { return P::kPairIsA ? stageD(s) : stageP(s); };
@@ -406,8 +406,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       origin(it.tile, &m0, &n0);
     }
     // Transposes trail the loads by kLag iterations: far enough behind for the
-    // data to have landed, early enough to stay ahead of the compute warps.
-    constexpr int kLag = P::kTransD ? kStages - 2 : 0;
+    // data to have landed, early enough to stay up to two iterations ahead of
+    // the compute warps. Deadlock-free: the load of iteration i waits for the
+    // consumers to release iteration i - kStages, and the transpose of
+    // iteration j = i - kLag waits for them to release j - kTransBufs; with
+    // kTransBufs >= kStages - kLag both point at iterations the consumers can
+    // finish without this transpose.
+    constexpr int kLag = P::kTrans ? kStages - 3 : 0;
+    static_assert(!P::kTrans || kTransBufs >= kStages - kLag, "transposed ring too small");
     for (int i = 0; i < total + kLag; ++i) {
       if (i < total) {
         const int s = i % kStages;
@@ -423,7 +429,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           }
         } else {
           if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
-          copyTile<kTA, kTB>(p, stageA(s), stageB(s), m0, n0, k0, pt);
+          copyOperand<P::kAExt, P::kA == Layout::kKX>(p.a, p.lda, p.m, p.k, stageA(s), m0, k0,
+                                                       pt, p.a_vec);
+          copyOperand<P::kBExt, P::kB == Layout::kKX>(p.b, p.ldb, p.n, p.k, stageB(s), n0, k0,
+                                                       pt, p.b_vec);
           cpAsyncArrive(&full[s]);
         }
         if (++kt == ke && ++idx < nitems) {
@@ -433,13 +442,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           origin(it.tile, &m0, &n0);
         }
       }
-      if constexpr (P::kTransD) {
+      if constexpr (P::kTrans) {
         const int j = i - kLag;
         if (j >= 0) {
           const int t = j % kTransBufs;
           wait(&full[j % kStages], (j / kStages) & 1);
           if (j >= kTransBufs) wait(&tempty[t], (j / kTransBufs - 1) & 1);
-          transposeDup(stageD(j % kStages), tbuf(t), pt);
+          if constexpr (P::kTransP) transposeKX<kBP>(stageP(j % kStages), tbufP(t), pt);
+          if constexpr (P::kTransD) transposeKX<kBD>(stageD(j % kStages), tbufD(t), pt);
           mbarArrive(&tfull[t]);
         }
       }
@@ -454,14 +464,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   const int wp = warp % kWarpsP, wd = warp / kWarpsP;
   const int lp = lane % 8, ld = lane / 8;
   const int p_base = wp * (8 * kTP) + lp * 4;
-  DupAddr da;
-  const int d_row0 = wd * 32 + ld * 4;  // [k][x] broadcast tile: first column
-  da.base = static_cast<uint32_t>(d_row0);
-#pragma unroll
-  for (int c = 0; c < 4; ++c) da.chunk[c] = 0;
-  static_assert(P::kCompD == Layout::kXK, "compute reads [k][x] broadcast tiles");
-  auto dCoord = [&](int j) { return d_row0 + (j & 3) + 16 * (j >> 2); };
-  auto pCoord = [&](int i) { return p_base + (i & 3) + 32 * (i >> 2); };
+  const int d_base = wd * 32 + ld * 4;
   bool ok = true;
   auto wait = [&](uint64_t *bar, int parity) {
     if (ok) ok = mbarWait(bar, static_cast<uint32_t>(parity), p.err);
@@ -474,42 +477,56 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
 
   const float alpha = p.alpha, beta = p.beta;
-  // C = alpha * acc (+ beta * C) for the tile at (m0, n0).
-  auto storeTile = [&](int m0, int n0) {
-    if constexpr (P::kPairIsA) {
-      const bool vec = m0 + P::kBM <= p.m && n0 + P::kBN <= p.n && (p.ldc % 4 == 0) &&
-                       (reinterpret_cast<uintptr_t>(p.c) % 16 == 0);
-      if (vec) {
+  const bool c_vec = (p.ldc % 4 == 0) && (reinterpret_cast<uintptr_t>(p.c) % 16 == 0);
+  // C = alpha * acc (+ beta * C) for the tile at (m0, n0). The thread's
+  // values come in groups of four consecutive rows of one column (P = A: four
+  // consecutive P coordinates; P = B: four consecutive D coordinates); a group
+  // inside the matrix is one float4 access when C allows it.
+  auto storeGroup = [&](int row, int col, float v0, float v1, float v2, float v3) {
+    if (col >= p.n || row >= p.m) return;
+    float *cp = p.c + static_cast<size_t>(col) * p.ldc + row;
+    if (c_vec && row + 3 < p.m) {
+      float4 cv = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+      if constexpr (kBeta != Beta::kZero) cv = *reinterpret_cast<const float4 *>(cp);
+      float4 out;
+      out.x = epilogueValue<kBeta>(v0, alpha, beta, cv.x);
+      out.y = epilogueValue<kBeta>(v1, alpha, beta, cv.y);
+      out.z = epilogueValue<kBeta>(v2, alpha, beta, cv.z);
+      out.w = epilogueValue<kBeta>(v3, alpha, beta, cv.w);
+      *reinterpret_cast<float4 *>(cp) = out;
+      return;
+    }
+    const float v[4] = {v0, v1, v2, v3};
 #pragma unroll
-        for (int j = 0; j < kTD; ++j) {
-          float *col = p.c + static_cast<size_t>(n0 + dCoord(j)) * p.ldc + m0 + p_base;
-#pragma unroll
-          for (int q = 0; q < kTP / 4; ++q) {
-            const float2 lo = acc[2 * q][j], hi = acc[2 * q + 1][j];
-            float4 cv = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
-            if constexpr (kBeta != Beta::kZero) cv = *reinterpret_cast<const float4 *>(col + 32 * q);
-            float4 out;
-            out.x = epilogueValue<kBeta>(lo.x, alpha, beta, cv.x);
-            out.y = epilogueValue<kBeta>(lo.y, alpha, beta, cv.y);
-            out.z = epilogueValue<kBeta>(hi.x, alpha, beta, cv.z);
-            out.w = epilogueValue<kBeta>(hi.y, alpha, beta, cv.w);
-            *reinterpret_cast<float4 *>(col + 32 * q) = out;
-          }
-        }
-        return;
+    for (int e = 0; e < 4; ++e) {
+      if (row + e < p.m) {
+        const float cv = kBeta == Beta::kZero ? 0.0F : cp[e];
+        cp[e] = epilogueValue<kBeta>(v[e], alpha, beta, cv);
       }
     }
+  };
+  auto storeTile = [&](int m0, int n0) {
+    if constexpr (P::kPairIsA) {
 #pragma unroll
-    for (int j = 0; j < kTD; ++j) {
+      for (int j = 0; j < kTD; ++j) {
+        const int col = n0 + d_base + (j & 3) + 16 * (j >> 2);
+#pragma unroll
+        for (int q = 0; q < kTP / 4; ++q) {
+          const float2 lo = acc[2 * q][j], hi = acc[2 * q + 1][j];
+          storeGroup(m0 + p_base + 32 * q, col, lo.x, lo.y, hi.x, hi.y);
+        }
+      }
+    } else {
 #pragma unroll
       for (int i = 0; i < kTP; ++i) {
-        const int row = P::kPairIsA ? m0 + pCoord(i) : m0 + dCoord(j);
-        const int col = P::kPairIsA ? n0 + dCoord(j) : n0 + pCoord(i);
-        if (row < p.m && col < p.n) {
-          float *cp = p.c + static_cast<size_t>(col) * p.ldc + row;
-          const float a = (i & 1) ? acc[i >> 1][j].y : acc[i >> 1][j].x;
-          const float cv = kBeta == Beta::kZero ? 0.0F : *cp;
-          *cp = epilogueValue<kBeta>(a, alpha, beta, cv);
+        const int col = n0 + p_base + (i & 3) + 32 * (i >> 2);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            v[e] = (i & 1) ? acc[i >> 1][4 * h + e].y : acc[i >> 1][4 * h + e].x;
+          storeGroup(m0 + d_base + 16 * h, col, v[0], v[1], v[2], v[3]);
         }
       }
     }
@@ -549,13 +566,18 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   for (int g = 0; g < total; ++g) {
     const int s = g % kStages;
     const int t = g % kTransBufs;
-    wait(&full[s], (g / kStages) & 1);
-    if constexpr (P::kTransD) wait(&tfull[t], (g / kTransBufs) & 1);
-    computeStage<P::kCompD>(stageP(s), P::kTransD ? tbuf(t) : stageD(s), p_base, da, acc);
+    // With a transposed operand, tfull[t] implies full[s]: every producer
+    // thread waited for stage s to land before transposing it and arriving
+    // on tfull[t] (release), so acquiring tfull[t] also makes the stage's TMA
+    // or cp.async data visible. One wait per iteration instead of two.
+    if constexpr (P::kTrans) wait(&tfull[t], (g / kTransBufs) & 1);
+    else wait(&full[s], (g / kStages) & 1);
+    computeStage(P::kTransP ? tbufP(t) : stageP(s), P::kTransD ? tbufD(t) : stageD(s), p_base,
+                 d_base, acc);
     __syncwarp();
     if (lane == 0) {
       mbarArrive(&empty[s]);
-      if constexpr (P::kTransD) mbarArrive(&tempty[t]);
+      if constexpr (P::kTrans) mbarArrive(&tempty[t]);
     }
 
     if (++c_kt == c_ke) {
