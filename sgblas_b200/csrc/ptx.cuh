@@ -53,8 +53,23 @@ __device__ __forceinline__ bool mbarTryWait(uint64_t *bar, uint32_t parity) {
   return done != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
+// Non-blocking test of phase completion.
+__device__ __forceinline__ bool mbarTestWait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smemAddr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete. The common
+// case -- the phase completed long ago -- costs one non-blocking test.
 __device__ __forceinline__ bool mbarWait(uint64_t *bar, uint32_t parity, unsigned *err) {
+  if (mbarTestWait(bar, parity)) return true;
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbarTryWait(bar, parity)) return true;
   }
