@@ -52,6 +52,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--size", type=int, default=4096, help="N=1 square size (4096 headline)")
+    ap.add_argument("--shape", type=str, default=None,
+                    help="N=1 M,N,K (default: --size cubed); e.g. 8192,8192,256 for config 4")
+    ap.add_argument("--beta", type=float, default=0.0, help="N=1 beta (config 4 uses 1)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
@@ -260,8 +263,12 @@ def run_single(args) -> None:
     torch.cuda.set_device(dev)
     props = torch.cuda.get_device_properties(dev)
     sms = props.multi_processor_count
-    m = n = k = args.size
-    lda = ldb = ldc = m
+    if args.shape:
+        m, n, k = (int(v) for v in args.shape.split(","))
+    else:
+        m = n = k = args.size
+    beta = args.beta
+    lda, ldb, ldc = m, max(k, 1), m   # column-major NN, tight (ldb >= k)
     flops = 2.0 * m * n * k
 
     rng = np.random.default_rng(1)
@@ -278,7 +285,7 @@ def run_single(args) -> None:
     h.set_stream(stream)
 
     def launch():
-        h.sgemm(0, 0, m, n, k, 1.0, da, lda, db, ldb, 0.0, dc, ldc)
+        h.sgemm(0, 0, m, n, k, 1.0, da, lda, db, ldb, beta, dc, ldc)
 
     with torch.cuda.stream(stream):
         for _ in range(warmup):
@@ -306,7 +313,7 @@ def run_single(args) -> None:
 
     mhz = clocks["sm_mhz"] or 1965.0
     peak = fp32_peak_tflops(sms, mhz)
-    traffic = profile_traffic(f"sgemm_nn_{m}.md")
+    traffic = profile_traffic(f"sgemm_nn_{m}x{n}x{k}.md")  # DRAM bytes per launch (ncu)
     roofline = {"bound": "fp32_fma", "achieved": value, "peak": peak, "unit": UNIT,
                 "frac": value / peak, "traffic": traffic,
                 "peak_source": f"{sms} SMs x {FP32_LANES_PER_SM} FP32 lanes x 2 x {mhz:.0f} MHz "
@@ -314,15 +321,18 @@ def run_single(args) -> None:
                                "MEASURED_PEAKS.json has no FP32 CUDA-core figure",
                 "frac_of_max_clock": value / fp32_peak_tflops(sms, 1965.0),
                 "algorithmic_flops_per_launch": flops,
-                "algorithmic_bytes_per_launch": 4.0 * (m * k + k * n + m * n)}
+                "algorithmic_bytes_per_launch": 4.0 * (m * k + k * n + m * n * (2 if beta else 1)),
+                "hbm_gbs_algorithmic": 4.0 * (m * k + k * n + m * n * (2 if beta else 1)) /
+                                       (total_s / steps) / 1e9}
 
     out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": steps,
            "warmup": warmup, "ms_per_step": 1e3 * total_s / steps, "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None,
            "vs_published_a100": value / 17.736,
            "dtype": "f32", "data": "synthetic",
-           "config": {"workload": f"sgemm NN {m}x{n}x{k} column-major alpha=1 beta=0 "
-                                  "(BASELINE configs[1])",
+           "config": {"workload": f"sgemm NN {m}x{n}x{k} column-major alpha=1 beta={beta:g}" +
+                                  (" (BASELINE configs[1])" if (m, n, k, beta) == (4096, 4096, 4096, 0.0)
+                                   else ""),
                       "m": m, "n": n, "k": k, "lda": lda, "ldb": ldb, "ldc": ldc,
                       "inputs": "uniform[-1,1) float32 (numpy seeds 1: A,B; 2: C)",
                       "l2": "flushed before every timed step (256 MiB write outside the "
@@ -334,9 +344,9 @@ def run_single(args) -> None:
         try:
             cb = Cublas()
             cb.set_stream(stream)
-            dc2 = torch.empty_like(dc)
+            dc2 = dc.clone()
             for _ in range(warmup):
-                cb.sgemm(0, 0, m, n, k, 1.0, da.data_ptr(), lda, db.data_ptr(), ldb, 0.0,
+                cb.sgemm(0, 0, m, n, k, 1.0, da.data_ptr(), lda, db.data_ptr(), ldb, beta,
                          dc2.data_ptr(), ldc)
             cev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(steps)]
@@ -345,7 +355,7 @@ def run_single(args) -> None:
                     flush.zero_()
                     cev[i][0].record(stream)
                     st = cb.sgemm(0, 0, m, n, k, 1.0, da.data_ptr(), lda, db.data_ptr(), ldb,
-                                  0.0, dc2.data_ptr(), ldc)
+                                  beta, dc2.data_ptr(), ldc)
                     cev[i][1].record(stream)
             torch.cuda.synchronize()
             assert st == 0
@@ -360,19 +370,21 @@ def run_single(args) -> None:
             out["cublas_pedantic"] = {"unavailable": str(e)}
 
     if not args.no_e2e:
-        out["e2e"] = e2e_single(torch, sg, ha, hb, m, n, k, max(10, steps // 4), warmup)
+        out["e2e"] = e2e_single(torch, sg, ha, hb, hc, beta, m, n, k, max(10, steps // 4), warmup)
     if not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(ha, hb, m, n, k, lda, ldb, args.cpu_seconds)
     h.close()
     print(json.dumps(out), flush=True)
 
 
-def e2e_single(torch, sg, ha, hb, m, n, k, steps, warmup) -> dict:
+def e2e_single(torch, sg, ha, hb, hc, beta, m, n, k, steps, warmup) -> dict:
     """The metric through the public C ABI with host buffers: each step copies
-    A and B from pinned host memory, runs sgblasSgemm and copies C back.
-    Two device buffer sets; copies of step i+1 overlap the SGEMM of step i."""
+    A and B (and C when beta != 0) from pinned host memory, runs sgblasSgemm
+    and copies C back. Two device buffer sets; copies of step i+1 overlap the
+    SGEMM of step i."""
     pa = torch.from_numpy(ha).pin_memory()
     pb = torch.from_numpy(hb).pin_memory()
+    pc_in = torch.from_numpy(hc).pin_memory() if beta != 0.0 else None
     pc = torch.empty(m * n, dtype=torch.float32).pin_memory()
     sets = [(torch.empty(m * k, device="cuda"), torch.empty(k * n, device="cuda"),
              torch.empty(m * n, device="cuda")) for _ in range(2)]
@@ -396,7 +408,10 @@ def e2e_single(torch, sg, ha, hb, m, n, k, steps, warmup) -> dict:
             s_comp.wait_event(in_done[j])
             if i >= 2:
                 s_comp.wait_event(out_done[j])        # C of step i-2 has left
-            h.sgemm(0, 0, m, n, k, 1.0, da, m, db, k, 0.0, dc, m)
+            if pc_in is not None:                     # C is an input too
+                with torch.cuda.stream(s_comp):
+                    dc.copy_(pc_in, non_blocking=True)
+            h.sgemm(0, 0, m, n, k, 1.0, da, m, db, k, beta, dc, m)
             comp_done[j].record(s_comp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(comp_done[j])
@@ -414,7 +429,8 @@ def e2e_single(torch, sg, ha, hb, m, n, k, steps, warmup) -> dict:
     secs = start.elapsed_time(end) / 1e3
     h.close()
     return {"value": 2.0 * m * n * k * steps / secs / 1e12, "unit": UNIT,
-            "h2d_bytes_per_step": 4 * (m * k + k * n), "d2h_bytes_per_step": 4 * m * n,
+            "h2d_bytes_per_step": 4 * (m * k + k * n + (m * n if pc_in is not None else 0)),
+            "d2h_bytes_per_step": 4 * m * n,
             "steps": steps, "pipelining": "2 buffer sets; H2D, SGEMM and D2H on 3 streams"}
 
 
