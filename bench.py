@@ -247,7 +247,7 @@ def run_reference(args) -> None:
            "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
            "note": "the reference has no CPU SGEMM (src/sgemm_host.cpp:26-27 returns "
                    "NOT_SUPPORTED); its only CPU GEMM arithmetic is the FP64 oracle loop"}
-    print(json.dumps(out), flush=True)
+    emit(json.dumps(out))
 
 
 # ---------------------------------------------------------------------------
@@ -374,7 +374,7 @@ def run_single(args) -> None:
     if not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(ha, hb, m, n, k, lda, ldb, args.cpu_seconds)
     h.close()
-    print(json.dumps(out), flush=True)
+    emit(json.dumps(out))
 
 
 def e2e_single(torch, sg, ha, hb, hc, beta, m, n, k, steps, warmup) -> dict:
@@ -527,7 +527,7 @@ def run_sharded(args) -> None:
                "clocks": {"sm_mhz": mhz, "sm_max_mhz": max((x["sm_max_mhz"] or 0) for x in allc),
                           "reasons": reasons},
                "gpu_launches": steps, "e2e": e2e}
-        print(json.dumps(out), flush=True)
+        emit(json.dumps(out))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -586,7 +586,22 @@ def e2e_sharded(torch, dist, sg, mg, rank, M, n_loc, K, flops, steps) -> dict:
                           "bytes are whole-job totals (A once on rank 0, B and C over all ranks)"}
 
 
+_RESULT_FD = None
+
+
+def emit(line: str) -> None:
+    """Writes the one result line to the process's real stdout (everything
+    else -- NCCL's banner, library messages -- was redirected to stderr)."""
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, (line + "\n").encode())
+
+
 def main():
+    global _RESULT_FD
+    # Keep stdout for the single JSON line: libraries that print (NCCL's
+    # version banner under NCCL_DEBUG=VERSION) go to stderr instead.
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     args = parse_args()
     sys.path.insert(0, str(ROOT))
     if args.impl == "reference":
