@@ -13,13 +13,14 @@
 
 namespace sgblas::detail {
 
-template <bool kTA, bool kTB, bool kPairIsA, kern::Beta kBeta, kern::Src kSrc>
+template <int kTP, bool kTA, bool kTB, bool kPairIsA, kern::Beta kBeta, kern::Src kSrc>
 sgblasStatus_t launchTiles(kern::GemmParams p, const Scratch &scratch, int device,
                            cudaStream_t stream) {
-  using Plan = kern::Plan<kTA, kTB, kPairIsA>;
-  auto kernel = kern::sgemmKernel<kTA, kTB, kPairIsA, kBeta, kSrc>;
+  using Plan = kern::Plan<kTA, kTB, kPairIsA, kTP>;
+  using G = kern::Geo<kTP>;
+  auto kernel = kern::sgemmKernel<kTP, kTA, kTB, kPairIsA, kBeta, kSrc>;
   static std::atomic<uint64_t> configured{0};
-  if (!configureKernel(reinterpret_cast<const void *>(kernel), device, kern::kSmemBytes,
+  if (!configureKernel(reinterpret_cast<const void *>(kernel), device, G::kSmemBytes,
                        &configured))
     return SGBLAS_STATUS_EXECUTION_FAILED;
   p.tiles_m = (p.m + Plan::kBM - 1) / Plan::kBM;
@@ -34,7 +35,7 @@ sgblasStatus_t launchTiles(kern::GemmParams p, const Scratch &scratch, int devic
   Schedule s = makeSchedule(tiles, p.kiters, sms);
   bool used_handle_workspace = false;
   if (s.sk_tiles > 0) {
-    const size_t need = kCounterRegionBytes + 2 * static_cast<size_t>(s.grid) * kSlotBytes;
+    const size_t need = kCounterRegionBytes + 2 * static_cast<size_t>(s.grid) * G::kSlotBytes;
     const bool counters_fit = static_cast<size_t>(s.sk_tiles) * sizeof(int) <= kCounterRegionBytes;
     unsigned char *base = nullptr;
     if (scratch.fixed != nullptr) {
@@ -66,7 +67,7 @@ sgblasStatus_t launchTiles(kern::GemmParams p, const Scratch &scratch, int devic
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(s.grid));
   cfg.blockDim = dim3(kern::kBlockThreads);
-  cfg.dynamicSmemBytes = kern::kSmemBytes;
+  cfg.dynamicSmemBytes = G::kSmemBytes;
   cfg.stream = stream;
   const sgblasStatus_t st = launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));
   if (st == SGBLAS_STATUS_SUCCESS && used_handle_workspace &&
@@ -75,25 +76,25 @@ sgblasStatus_t launchTiles(kern::GemmParams p, const Scratch &scratch, int devic
   return st;
 }
 
-template <bool kTA, bool kTB, bool kPairIsA, kern::Src kSrc>
+template <int kTP, bool kTA, bool kTB, bool kPairIsA, kern::Src kSrc>
 sgblasStatus_t launchByBeta(const kern::GemmParams &p, const Scratch &scratch, int device,
                             cudaStream_t stream) {
   using kern::Beta;
   if (p.beta == 0.0F)
-    return launchTiles<kTA, kTB, kPairIsA, Beta::kZero, kSrc>(p, scratch, device, stream);
+    return launchTiles<kTP, kTA, kTB, kPairIsA, Beta::kZero, kSrc>(p, scratch, device, stream);
   if (p.beta == 1.0F)
-    return launchTiles<kTA, kTB, kPairIsA, Beta::kOne, kSrc>(p, scratch, device, stream);
-  return launchTiles<kTA, kTB, kPairIsA, Beta::kGeneral, kSrc>(p, scratch, device, stream);
+    return launchTiles<kTP, kTA, kTB, kPairIsA, Beta::kOne, kSrc>(p, scratch, device, stream);
+  return launchTiles<kTP, kTA, kTB, kPairIsA, Beta::kGeneral, kSrc>(p, scratch, device, stream);
 }
 
 // TMA when both bases are 16-byte aligned and both leading dimensions are a
 // multiple of 16 bytes (and the driver accepts the descriptors); otherwise
 // cp.async, per operand in the widest size (16, 8 or 4 bytes) its base and
 // leading dimension allow. Each operand is staged in its natural layout.
-template <bool kTA, bool kTB, bool kPairIsA>
+template <int kTP, bool kTA, bool kTB, bool kPairIsA>
 sgblasStatus_t launchOriented(kern::GemmParams p, const Scratch &scratch, int device,
                               cudaStream_t stream) {
-  using Plan = kern::Plan<kTA, kTB, kPairIsA>;
+  using Plan = kern::Plan<kTA, kTB, kPairIsA, kTP>;
   using kern::Layout;
   if (aligned16(p.a) && aligned16(p.b) && p.lda % 4 == 0 && p.ldb % 4 == 0) {
     const bool a_kx = Plan::kA == Layout::kKX;
@@ -103,7 +104,7 @@ sgblasStatus_t launchOriented(kern::GemmParams p, const Scratch &scratch, int de
                      a_kx ? bk : Plan::kAExt, a_kx ? Plan::kAExt : bk, a_kx) &&
         encodeMatrix(&p.tma_b, p.b, kTB ? p.n : p.k, kTB ? p.k : p.n, p.ldb,
                      b_kx ? bk : Plan::kBExt, b_kx ? Plan::kBExt : bk, b_kx))
-      return launchByBeta<kTA, kTB, kPairIsA, kern::Src::kTma>(p, scratch, device, stream);
+      return launchByBeta<kTP, kTA, kTB, kPairIsA, kern::Src::kTma>(p, scratch, device, stream);
   }
   // Widest cp.async the operand's alignment allows.
   auto vec = [](const float *ptr, int ld) {
@@ -114,25 +115,39 @@ sgblasStatus_t launchOriented(kern::GemmParams p, const Scratch &scratch, int de
   };
   p.a_vec = vec(p.a, p.lda);
   p.b_vec = vec(p.b, p.ldb);
-  return launchByBeta<kTA, kTB, kPairIsA, kern::Src::kCopy>(p, scratch, device, stream);
+  return launchByBeta<kTP, kTA, kTB, kPairIsA, kern::Src::kCopy>(p, scratch, device, stream);
 }
 
-// Orientation: the pair operand spans 256 rows of its side of C, the broadcast
-// operand 128. Choose the orientation with less padded tile area, then the one
-// that transposes fewer elements per k step.
-template <bool kTA, bool kTB>
-sgblasStatus_t launchMode(kern::GemmParams p, const Scratch &scratch, int device,
-                          cudaStream_t stream) {
-  using PA = kern::Plan<kTA, kTB, true>;
-  using PB = kern::Plan<kTA, kTB, false>;
+// Tile size and orientation. The pair operand spans 256 (kTP = 16) or 128
+// (kTP = 8) rows of its side of C, the broadcast operand 128. Large tiles are
+// used when they give at least one tile per SM; otherwise 128 x 128 tiles
+// spread a small problem over more SMs with less stream-K splitting. Among
+// orientations: less padded tile area, then fewer transposed elements per k
+// step.
+template <int kTP, bool kTA, bool kTB>
+sgblasStatus_t launchSized(kern::GemmParams p, const Scratch &scratch, int device,
+                           cudaStream_t stream) {
+  using PA = kern::Plan<kTA, kTB, true, kTP>;
+  using PB = kern::Plan<kTA, kTB, false, kTP>;
   auto padded = [](long long x, long long t) { return (x + t - 1) / t * t; };
   const long long area_a = padded(p.m, PA::kBM) * padded(p.n, PA::kBN);
   const long long area_b = padded(p.m, PB::kBM) * padded(p.n, PB::kBN);
-  constexpr int trans_a = (PA::kTransP ? kern::kBP : 0) + (PA::kTransD ? kern::kBD : 0);
-  constexpr int trans_b = (PB::kTransP ? kern::kBP : 0) + (PB::kTransD ? kern::kBD : 0);
+  constexpr int trans_a = (PA::kTransP ? PA::kBP : 0) + (PA::kTransD ? kern::kBD : 0);
+  constexpr int trans_b = (PB::kTransP ? PB::kBP : 0) + (PB::kTransD ? kern::kBD : 0);
   const bool pair_is_a = area_a < area_b || (area_a == area_b && trans_a <= trans_b);
-  if (pair_is_a) return launchOriented<kTA, kTB, true>(p, scratch, device, stream);
-  return launchOriented<kTA, kTB, false>(p, scratch, device, stream);
+  if (pair_is_a) return launchOriented<kTP, kTA, kTB, true>(p, scratch, device, stream);
+  return launchOriented<kTP, kTA, kTB, false>(p, scratch, device, stream);
+}
+
+template <bool kTA, bool kTB>
+sgblasStatus_t launchMode(kern::GemmParams p, const Scratch &scratch, int device,
+                          cudaStream_t stream) {
+  auto tiles = [&](long long bm, long long bn) {
+    return ((p.m + bm - 1) / bm) * ((p.n + bn - 1) / bn);
+  };
+  const long long large = std::min(tiles(256, 128), tiles(128, 256));
+  if (large >= smCount(device)) return launchSized<16, kTA, kTB>(p, scratch, device, stream);
+  return launchSized<8, kTA, kTB>(p, scratch, device, stream);
 }
 
 }  // namespace sgblas::detail

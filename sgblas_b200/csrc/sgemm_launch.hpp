@@ -45,7 +45,7 @@ Schedule makeSchedule(long long tiles, int kiters, int sms);
 // 512 SMs; the counter region has a fixed size so that the layout is the same
 // for every call (counters left at zero by one launch must never be
 // overlapped by another launch's slots).
-constexpr size_t kSlotBytes = size_t{kern::kThreads} * kern::kSlotFloat4 * sizeof(float4);
+constexpr size_t kSlotBytes = kern::Geo<16>::kSlotBytes;  // the largest slot (128 KiB)
 constexpr size_t kCounterRegionBytes = 4096;
 
 // Where a launch takes its stream-K scratch from.

@@ -51,14 +51,12 @@
 
 namespace sgblas::kern {
 
-constexpr int kBP = 256;   // pair-operand tile extent
 constexpr int kBD = 128;   // broadcast-operand tile extent
 constexpr int kBK = 16;    // k slice per pipeline stage
 constexpr int kStages = 6;
 constexpr int kTransBufs = 3;   // ring of transposed [k][x] tiles
-constexpr int kTP = 16;         // pair-operand elements per thread
 constexpr int kTD = 8;          // broadcast-operand elements per thread
-constexpr int kWarpsP = kBP / (8 * kTP);   // warps along P (8 lanes x kTP each)
+constexpr int kWarpsP = 2;      // warps along P (8 lanes x kTP each)
 constexpr int kWarpsD = kBD / 32;          // warps along D (4 lanes x 8 each)
 constexpr int kThreads = 32 * kWarpsP * kWarpsD;   // compute threads (256)
 constexpr int kConsumerWarps = kThreads / 32;
@@ -73,17 +71,29 @@ constexpr int kProducerRegs = 40;
 static_assert(kThreads * kConsumerRegs + kProducerThreads * kProducerRegs <=
                   kBlockThreads * kLaunchRegs,
               "register split exceeds the launch allocation");
-constexpr int kSlotFloat4 = kTP * kTD / 4;  // float4s per thread in a partial slot
-constexpr int kPairFloats = kBP * kBK;
 constexpr int kDupFloats = kBD * kBK;
-constexpr int kPairBytes = kPairFloats * 4;   // 16 KiB
 constexpr int kDupBytes = kDupFloats * 4;     // 8 KiB
-constexpr int kStageBytes = kPairBytes + kDupBytes;
-constexpr int kTransBytes = kTransBufs * kStageBytes;  // room for both operands
 constexpr int kBarrierBytes = 8 * (2 * kStages + 2 * kTransBufs);
 constexpr int kSmemAlign = 1024;
-constexpr int kSmemBytes = kStages * kStageBytes + kTransBytes + kBarrierBytes + kSmemAlign;
-static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+
+// Tile geometry by pair-operand elements per thread: kTP = 16 gives the
+// 256 (P) x 128 (D) tile used for large problems, kTP = 8 a 128 x 128 tile for
+// problems with too few large tiles to fill the GPU.
+template <int kTP_>
+struct Geo {
+  static constexpr int kTP = kTP_;
+  static constexpr int kBP = kWarpsP * 8 * kTP;   // pair-operand tile extent
+  static constexpr int kPairFloats = kBP * kBK;
+  static constexpr int kPairBytes = kPairFloats * 4;
+  static constexpr int kStageBytes = kPairBytes + kDupBytes;
+  static constexpr int kTransBytes = kTransBufs * kStageBytes;  // room for both operands
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kTransBytes + kBarrierBytes + kSmemAlign;
+  static constexpr int kSlotFloat4 = kTP * kTD / 4;  // float4s per thread in a partial slot
+  static constexpr size_t kSlotBytes = size_t{kThreads} * kSlotFloat4 * 16;
+  static_assert(kTP == 8 || kTP == 16, "per-thread pair extent");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+};
 
 enum class Beta { kZero, kOne, kGeneral };
 enum class Src { kTma, kCopy };
@@ -110,7 +120,7 @@ struct GemmParams {
   int dp_tiles;
   int sk_tiles;
   int sk_q, sk_r;
-  float4 *ws;         // 2 * grid partial-tile slots of kThreads * kSlotFloat4 float4
+  float4 *ws;         // 2 * grid partial-tile slots of Geo::kSlotBytes
   int *counters;      // sk_tiles arrival counters, zero between launches
   // cp.async path: floats per copy (1, 2 or 4) allowed by each operand's base
   // alignment and leading dimension.
@@ -166,8 +176,10 @@ __device__ __forceinline__ uint32_t kxOffset(int x, int k) {
 }
 
 // Operand roles, staged layouts and the tile shape that follows.
-template <bool kTA, bool kTB, bool kPairIsA_>
+template <bool kTA, bool kTB, bool kPairIsA_, int kTP>
 struct Plan {
+  using G = Geo<kTP>;
+  static constexpr int kBP = G::kBP;
   static constexpr bool kPairIsA = kPairIsA_;
   // Natural staged layout: [k][x] when x is the contiguous global dimension.
   static constexpr Layout kA = kTA ? Layout::kKX : Layout::kXK;
@@ -262,8 +274,10 @@ __device__ __forceinline__ void transposeKX(const float *src, float *dst, int ti
 
 // ---- the FFMA2 micro-kernel over one BK slice ------------------------------
 // sp: [k][kBP] pair tile, sd: [k][kBD] broadcast tile.
+template <int kTP>
 __device__ __forceinline__ void computeStage(const float *sp, const float *sd, int p_base,
                                              int d_base, float2 (&acc)[kTP / 2][kTD]) {
+  constexpr int kBP = Geo<kTP>::kBP;
 #pragma unroll
   for (int k = 0; k < kBK; k += 2) {
     float dv[2][kTD];
@@ -324,10 +338,16 @@ __device__ __forceinline__ float epilogueValue(float acc, float alpha, float bet
 // A wait that times out raises the device error flag; from then on that
 // thread skips its waits (results are garbage and flagged) but still runs
 // every loop to its end, so that no thread is left behind at a barrier.
-template <bool kTA, bool kTB, bool kPairIsA, Beta kBeta, Src kSrc>
+template <int kTP, bool kTA, bool kTB, bool kPairIsA, Beta kBeta, Src kSrc>
 __global__ void __launch_bounds__(kBlockThreads, 1)
     sgemmKernel(const __grid_constant__ GemmParams p) {
-  using P = Plan<kTA, kTB, kPairIsA>;
+  using P = Plan<kTA, kTB, kPairIsA, kTP>;
+  using G = typename P::G;
+  constexpr int kBP = G::kBP;
+  constexpr int kPairBytes = G::kPairBytes;
+  constexpr int kStageBytes = G::kStageBytes;
+  constexpr int kTransBytes = G::kTransBytes;
+  constexpr int kSlotFloat4 = G::kSlotFloat4;
   extern __shared__ unsigned char smem_raw[];
   __shared__ int last_arrival;
   // Align within the shared window by offsetting smem_raw itself: pointers
@@ -572,8 +592,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     // or cp.async data visible. One wait per iteration instead of two.
     if constexpr (P::kTrans) wait(&tfull[t], (g / kTransBufs) & 1);
     else wait(&full[s], (g / kStages) & 1);
-    computeStage(P::kTransP ? tbufP(t) : stageP(s), P::kTransD ? tbufD(t) : stageD(s), p_base,
-                 d_base, acc);
+    computeStage<kTP>(P::kTransP ? tbufP(t) : stageP(s), P::kTransD ? tbufD(t) : stageD(s),
+                      p_base, d_base, acc);
     __syncwarp();
     if (lane == 0) {
       mbarArrive(&empty[s]);
