@@ -17,6 +17,13 @@ extern "C" {
  * No counterpart in the reference (it has no device-side waits). */
 sgblasStatus_t sgblasGetDeviceErrors(unsigned *flags, int clear);
 
+/* Self-test of the kernels' bounded waits: a one-thread kernel waits on a
+ * barrier that nothing completes, giving up after `polls` polls. On return
+ * *timed_out is 1 when the wait gave up (and the device error flags then hold
+ * bit 0, which sgblasGetDeviceErrors reads and may clear); the device stays
+ * usable. Synchronizes the current device. No counterpart in the reference. */
+sgblasStatus_t sgblasSelfTestWaitTimeout(unsigned polls, int *timed_out);
+
 /* sgblasSgemm for callers that cannot allocate device memory (their process
  * or host owns the allocator, or forbids allocation after start-up). Same
  * arguments, semantics and status codes as sgblasSgemm, but instead of the

@@ -1,5 +1,6 @@
 // Device error word and the diagnostics entry point that reads it.
 #include "device.hpp"
+#include "ptx.cuh"
 
 #include <sgblas/sgblas_ext.h>
 
@@ -25,7 +26,50 @@ unsigned *deviceErrorWord(int device) {
   return static_cast<unsigned *>(address);
 }
 
+namespace {
+
+// Waits on an mbarrier that nothing will ever complete, with a short poll
+// limit: the wait must give up, raise the error flag and let the kernel
+// return normally. Reports whether the wait returned false.
+__global__ void waitTimeoutKernel(unsigned *err, unsigned polls, int *gave_up) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    kern::mbarInit(&bar, 1);
+    kern::fenceBarrierInit();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *gave_up = kern::mbarWait(&bar, 0, err, polls) ? 0 : 1;
+}
+
+}  // namespace
+
 }  // namespace sgblas::detail
+
+extern "C" sgblasStatus_t sgblasSelfTestWaitTimeout(unsigned polls, int *timed_out) {
+  if (timed_out == nullptr || polls == 0) return SGBLAS_STATUS_INVALID_VALUE;
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  }
+  unsigned *err = sgblas::detail::deviceErrorWord(device);
+  if (err == nullptr) return SGBLAS_STATUS_EXECUTION_FAILED;
+  int *flag = nullptr;
+  if (cudaMallocManaged(&flag, sizeof(int)) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return SGBLAS_STATUS_ALLOC_FAILED;
+  }
+  *flag = -1;
+  sgblas::detail::waitTimeoutKernel<<<1, 32>>>(err, polls, flag);
+  const cudaError_t e = cudaDeviceSynchronize();
+  *timed_out = *flag;
+  (void)cudaFree(flag);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  }
+  return SGBLAS_STATUS_SUCCESS;
+}
 
 extern "C" sgblasStatus_t sgblasGetDeviceErrors(unsigned *flags, int clear) {
   if (flags == nullptr) return SGBLAS_STATUS_INVALID_VALUE;

@@ -68,9 +68,10 @@ __device__ __forceinline__ bool mbarTestWait(uint64_t *bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity to complete. The common
 // case -- the phase completed long ago -- costs one non-blocking test.
-__device__ __forceinline__ bool mbarWait(uint64_t *bar, uint32_t parity, unsigned *err) {
+__device__ __forceinline__ bool mbarWait(uint64_t *bar, uint32_t parity, unsigned *err,
+                                         uint32_t limit = kSpinLimit) {
   if (mbarTestWait(bar, parity)) return true;
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbarTryWait(bar, parity)) return true;
   }
   if (err != nullptr) atomicOr(err, kErrBarrierTimeout);
@@ -119,6 +120,13 @@ __device__ __forceinline__ void tmaLoad2d(void *dst, const CUtensorMap *map, uin
 
 __device__ __forceinline__ void prefetchTensorMap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Asynchronous prefetch of [ptr, ptr + bytes) from global memory into L2.
+// ptr 16-byte aligned, bytes a non-zero multiple of 16; the range must lie
+// inside one allocation.
+__device__ __forceinline__ void prefetchL2Bulk(const void *ptr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(bytes) : "memory");
 }
 
 // 4-byte cp.async with zero fill: copies `bytes` (0 or 4) and zero-fills the

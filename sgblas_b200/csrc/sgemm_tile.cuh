@@ -418,12 +418,33 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     auto wait = [&](uint64_t *bar, int parity) {
       if (ok) ok = mbarWait(bar, static_cast<uint32_t>(parity), p.err);
     };
+    // With beta != 0 the epilogue of a whole tile reads its block of C. The
+    // producer prefetches that block into L2 when it starts loading the tile,
+    // a whole tile's main loop before the read: one column per thread, the
+    // 16-byte aligned interior of the in-range rows (never outside C).
+    auto prefetchC = [&](const Item &it, int tm0, int tn0) {
+      if constexpr (kBeta != Beta::kZero) {
+        if (it.kb != 0 || it.ke != p.kiters) return;
+        const int r1 = min(tm0 + P::kBM, p.m);
+#pragma unroll 1
+        for (int cc = pt; cc < P::kBN; cc += kProducerThreads) {
+          const int col = tn0 + cc;
+          if (col >= p.n) break;
+          const float *colp = p.c + static_cast<size_t>(col) * p.ldc;
+          const uintptr_t lo = (reinterpret_cast<uintptr_t>(colp + tm0) + 15) & ~uintptr_t{15};
+          const uintptr_t hi = reinterpret_cast<uintptr_t>(colp + r1) & ~uintptr_t{15};
+          if (hi > lo)
+            prefetchL2Bulk(reinterpret_cast<const void *>(lo), static_cast<uint32_t>(hi - lo));
+        }
+      }
+    };
     int idx = 0, kt, ke, m0, n0;
     {
       const Item it = itemAt(p, cta, 0);
       kt = it.kb;
       ke = it.ke;
       origin(it.tile, &m0, &n0);
+      prefetchC(it, m0, n0);
     }
     // Transposes trail the loads by kLag iterations: far enough behind for the
     // data to have landed, early enough to stay up to two iterations ahead of
@@ -460,6 +481,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           kt = it.kb;
           ke = it.ke;
           origin(it.tile, &m0, &n0);
+          prefetchC(it, m0, n0);
         }
       }
       if constexpr (P::kTrans) {
@@ -499,55 +521,82 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   const float alpha = p.alpha, beta = p.beta;
   const bool c_vec = (p.ldc % 4 == 0) && (reinterpret_cast<uintptr_t>(p.c) % 16 == 0);
   // C = alpha * acc (+ beta * C) for the tile at (m0, n0). The thread's
-  // values come in groups of four consecutive rows of one column (P = A: four
-  // consecutive P coordinates; P = B: four consecutive D coordinates); a group
-  // inside the matrix is one float4 access when C allows it.
-  auto storeGroup = [&](int row, int col, float v0, float v1, float v2, float v3) {
+  // values come in kGroups groups of four consecutive rows of one column
+  // (P = A: four consecutive P coordinates; P = B: four consecutive D
+  // coordinates); a group inside the matrix is one float4 access when C
+  // allows it. With beta != 0 the C reads of a batch of groups are all issued
+  // before any of its stores (the compiler cannot move a load of C past a
+  // store to C), so their latencies overlap; the producer has prefetched the
+  // block into L2 during the tile's main loop.
+  constexpr int kGroups = kTP * kTD / 4;
+  constexpr int kBatch = 8;
+  static_assert(kGroups % kBatch == 0, "epilogue batches");
+  auto groupAt = [&](int g, int m0, int n0, int *row, int *col, float v[4]) {
+    if constexpr (P::kPairIsA) {
+      const int j = g / (kTP / 4), q = g % (kTP / 4);
+      *col = n0 + d_base + (j & 3) + 16 * (j >> 2);
+      *row = m0 + p_base + 32 * q;
+      v[0] = acc[2 * q][j].x;
+      v[1] = acc[2 * q][j].y;
+      v[2] = acc[2 * q + 1][j].x;
+      v[3] = acc[2 * q + 1][j].y;
+    } else {
+      const int i = g / 2, h = g % 2;
+      *col = n0 + p_base + (i & 3) + 32 * (i >> 2);
+      *row = m0 + d_base + 16 * h;
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        v[e] = (i & 1) ? acc[i >> 1][4 * h + e].y : acc[i >> 1][4 * h + e].x;
+    }
+  };
+  auto loadGroup = [&](int row, int col) {
+    float4 cv = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+    if (col >= p.n || row >= p.m) return cv;
+    const float *cp = p.c + static_cast<size_t>(col) * p.ldc + row;
+    if (c_vec && row + 3 < p.m) return *reinterpret_cast<const float4 *>(cp);
+    cv.x = cp[0];
+    if (row + 1 < p.m) cv.y = cp[1];
+    if (row + 2 < p.m) cv.z = cp[2];
+    if (row + 3 < p.m) cv.w = cp[3];
+    return cv;
+  };
+  auto storeGroup = [&](int row, int col, const float v[4], float4 cv) {
     if (col >= p.n || row >= p.m) return;
     float *cp = p.c + static_cast<size_t>(col) * p.ldc + row;
+    float4 out;
+    out.x = epilogueValue<kBeta>(v[0], alpha, beta, cv.x);
+    out.y = epilogueValue<kBeta>(v[1], alpha, beta, cv.y);
+    out.z = epilogueValue<kBeta>(v[2], alpha, beta, cv.z);
+    out.w = epilogueValue<kBeta>(v[3], alpha, beta, cv.w);
     if (c_vec && row + 3 < p.m) {
-      float4 cv = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
-      if constexpr (kBeta != Beta::kZero) cv = *reinterpret_cast<const float4 *>(cp);
-      float4 out;
-      out.x = epilogueValue<kBeta>(v0, alpha, beta, cv.x);
-      out.y = epilogueValue<kBeta>(v1, alpha, beta, cv.y);
-      out.z = epilogueValue<kBeta>(v2, alpha, beta, cv.z);
-      out.w = epilogueValue<kBeta>(v3, alpha, beta, cv.w);
       *reinterpret_cast<float4 *>(cp) = out;
       return;
     }
-    const float v[4] = {v0, v1, v2, v3};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      if (row + e < p.m) {
-        const float cv = kBeta == Beta::kZero ? 0.0F : cp[e];
-        cp[e] = epilogueValue<kBeta>(v[e], alpha, beta, cv);
-      }
-    }
+    cp[0] = out.x;
+    if (row + 1 < p.m) cp[1] = out.y;
+    if (row + 2 < p.m) cp[2] = out.z;
+    if (row + 3 < p.m) cp[3] = out.w;
   };
   auto storeTile = [&](int m0, int n0) {
-    if constexpr (P::kPairIsA) {
 #pragma unroll
-      for (int j = 0; j < kTD; ++j) {
-        const int col = n0 + d_base + (j & 3) + 16 * (j >> 2);
+    for (int g0 = 0; g0 < kGroups; g0 += kBatch) {
+      float4 cv[kBatch];
 #pragma unroll
-        for (int q = 0; q < kTP / 4; ++q) {
-          const float2 lo = acc[2 * q][j], hi = acc[2 * q + 1][j];
-          storeGroup(m0 + p_base + 32 * q, col, lo.x, lo.y, hi.x, hi.y);
+      for (int b = 0; b < kBatch; ++b) {
+        cv[b] = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+        if constexpr (kBeta != Beta::kZero) {
+          int row, col;
+          float v[4];
+          groupAt(g0 + b, m0, n0, &row, &col, v);
+          cv[b] = loadGroup(row, col);
         }
       }
-    } else {
 #pragma unroll
-      for (int i = 0; i < kTP; ++i) {
-        const int col = n0 + p_base + (i & 3) + 32 * (i >> 2);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float v[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            v[e] = (i & 1) ? acc[i >> 1][4 * h + e].y : acc[i >> 1][4 * h + e].x;
-          storeGroup(m0 + d_base + 16 * h, col, v[0], v[1], v[2], v[3]);
-        }
+      for (int b = 0; b < kBatch; ++b) {
+        int row, col;
+        float v[4];
+        groupAt(g0 + b, m0, n0, &row, &col, v);
+        storeGroup(row, col, v, cv[b]);
       }
     }
   };

@@ -261,3 +261,22 @@ def test_matches_reference_golden_outputs(cuda, handle):
         _, mag = oracle.sgemm_f64_points(case.transa, case.transb, case.k, case.alpha, a,
                                          case.lda, b, case.ldb, case.beta, c, case.ldc, rows, cols)
         assert np.all(np.abs(ours - theirs) <= 2 * oracle.tol_north_star(case.k, mag)), case.name
+
+
+# ---- failure detection: bounded waits ------------------------------------------
+def test_bounded_wait_times_out_and_reports(cuda):
+    """A wait on a barrier nothing completes gives up, raises the device error
+    flag and returns; the context stays usable (an SGEMM right after is exact)."""
+    import ctypes
+    assert sg.get_device_errors(clear=True) == 0
+    timed_out = ctypes.c_int(-1)
+    assert sg.lib.sgblasSelfTestWaitTimeout(2000, ctypes.byref(timed_out)) == 0
+    assert timed_out.value == 1
+    assert sg.get_device_errors(clear=True) & 1
+    assert sg.get_device_errors(clear=True) == 0
+    with sg.Handle() as h:
+        case = C.cfg1()
+        a, b, c = C.cfg_inputs(case, 0, -1)
+        status, out = run_sgemm(cuda, h, case, a, b, c)
+        assert status == 0
+        _assert(check_full(case, a, b, c, out), "after timeout")
