@@ -164,12 +164,31 @@ bool ensureWorkspace(sgblasContext *ctx, size_t need, int device, cudaStream_t s
     }
     return true;
   }
-  releaseWorkspace(ctx);
+  if (ctx->workspace != nullptr && ctx->workspace_device == device) {
+    // Growing: free the old buffer stream-ordered after its last user, so the
+    // call does not block the host.
+    const auto ev = static_cast<cudaEvent_t>(ctx->workspace_event);
+    const bool ordered = ev == nullptr || cudaStreamWaitEvent(stream, ev, 0) == cudaSuccess;
+    if (!ordered || cudaFreeAsync(ctx->workspace, stream) != cudaSuccess) {
+      (void)cudaGetLastError();
+      releaseWorkspace(ctx);
+    } else {
+      if (ev != nullptr) (void)cudaEventDestroy(ev);  // released once it completes
+      ctx->workspace = nullptr;
+      ctx->workspace_bytes = 0;
+      ctx->workspace_device = -1;
+      ctx->workspace_event = nullptr;
+    }
+  } else {
+    releaseWorkspace(ctx);
+  }
   if (cudaSetDevice(device) != cudaSuccess) {
     (void)cudaGetLastError();
     return false;
   }
-  const size_t bytes = std::max(need, size_t{64} << 20);  // room for later, larger calls
+  // Room for later, larger calls: at least 64 MiB, and a quarter more than
+  // asked when growing past that.
+  const size_t bytes = std::max(need + need / 4, size_t{64} << 20);
   void *ws = nullptr;
   cudaEvent_t ev = nullptr;
   if (cudaMallocAsync(&ws, bytes, stream) != cudaSuccess) {
@@ -177,7 +196,7 @@ bool ensureWorkspace(sgblasContext *ctx, size_t need, int device, cudaStream_t s
     return false;
   }
   // Counters must start at zero; every launch leaves them at zero again.
-  if (cudaMemsetAsync(ws, 0, bytes, stream) != cudaSuccess ||
+  if (cudaMemsetAsync(ws, 0, std::min(bytes, kCounterRegionBytes), stream) != cudaSuccess ||
       cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
     (void)cudaGetLastError();
     (void)cudaFreeAsync(ws, stream);
@@ -228,11 +247,55 @@ sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOpe
   Scratch scratch;
   scratch.ctx = ctx;
 
-  const bool tA = ta == SGBLAS_OP_T, tB = tb == SGBLAS_OP_T;
-  if (!tA && !tB) return launchMode<false, false>(p, scratch, device, stream);
-  if (!tA && tB) return launchMode<false, true>(p, scratch, device, stream);
-  if (tA && !tB) return launchMode<true, false>(p, scratch, device, stream);
-  return launchMode<true, true>(p, scratch, device, stream);
+  bool tA = ta == SGBLAS_OP_T, tB = tb == SGBLAS_OP_T;
+  // An operand TMA cannot read in place (base not 16-byte aligned, or ld not
+  // a multiple of 4 floats) is copied into the workspace as an x-contiguous
+  // matrix (A: m x k, as for op N; B: n x k, as for op T) with an aligned
+  // leading dimension, and the product runs on TMA staging. Without a
+  // workspace the tile kernel stages it with cp.async instead.
+  const bool pack_a = !(aligned16(a) && lda % 4 == 0);
+  const bool pack_b = !(aligned16(b) && ldb % 4 == 0);
+  bool packed = false;
+  if (pack_a || pack_b) {
+    const int sms = smCount(device);
+    if (sms <= 0) return SGBLAS_STATUS_EXECUTION_FAILED;
+    auto roundUp = [](size_t v, size_t q) { return (v + q - 1) / q * q; };
+    const int ldp_a = static_cast<int>(roundUp(static_cast<size_t>(m), kPackLdMultiple));
+    const int ldp_b = static_cast<int>(roundUp(static_cast<size_t>(n), kPackLdMultiple));
+    const size_t off_a = roundUp(streamKRegionBytes(sms), kPackAlign);
+    const size_t bytes_a = pack_a ? static_cast<size_t>(ldp_a) * k * sizeof(float) : 0;
+    const size_t off_b = roundUp(off_a + bytes_a, kPackAlign);
+    const size_t bytes_b = pack_b ? static_cast<size_t>(ldp_b) * k * sizeof(float) : 0;
+    if (ldp_a >= m && ldp_b >= n && ensureWorkspace(ctx, off_b + bytes_b, device, stream)) {
+      auto *ws = static_cast<unsigned char *>(ctx->workspace);
+      if (pack_a) {
+        auto *dst = reinterpret_cast<float *>(ws + off_a);
+        const sgblasStatus_t st = launchPack(a, lda, tA, m, k, dst, ldp_a, sms, stream);
+        if (st != SGBLAS_STATUS_SUCCESS) return st;
+        p.a = dst;
+        p.lda = ldp_a;
+        tA = false;
+      }
+      if (pack_b) {
+        auto *dst = reinterpret_cast<float *>(ws + off_b);
+        const sgblasStatus_t st = launchPack(b, ldb, !tB, n, k, dst, ldp_b, sms, stream);
+        if (st != SGBLAS_STATUS_SUCCESS) return st;
+        p.b = dst;
+        p.ldb = ldp_b;
+        tB = true;
+      }
+      packed = true;
+    }
+  }
+  sgblasStatus_t st;
+  if (!tA && !tB) st = launchMode<false, false>(p, scratch, device, stream);
+  else if (!tA && tB) st = launchMode<false, true>(p, scratch, device, stream);
+  else if (tA && !tB) st = launchMode<true, false>(p, scratch, device, stream);
+  else st = launchMode<true, true>(p, scratch, device, stream);
+  // The product read the packed operands: later users of the workspace wait.
+  if (st == SGBLAS_STATUS_SUCCESS && packed && !markWorkspaceUse(ctx, stream))
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  return st;
 }
 
 }  // namespace

@@ -55,6 +55,21 @@ struct Scratch {
   size_t fixed_bytes = 0;
 };
 
+// Operand staging copies in the handle workspace (sgemm_pack.cu). The
+// workspace layout with packed operands is [counters | 2*SMs slots | packed
+// A | packed B], so the stream-K part keeps the same offsets on every call.
+constexpr size_t kPackAlign = 256;
+constexpr int kPackLdMultiple = 32;  // floats: 128-byte aligned columns
+inline size_t streamKRegionBytes(int sms) {
+  return kCounterRegionBytes + 2 * static_cast<size_t>(sms) * kSlotBytes;
+}
+// Writes the operand whose element (x, k) is at src[x + k*ld]
+// (k_contiguous false) or src[k + x*ld] (k_contiguous true) to dst as an
+// rows_x x cols_k column-major matrix with leading dimension ldp (a multiple
+// of 4; dst 16-byte aligned).
+sgblasStatus_t launchPack(const float *src, int ld, bool k_contiguous, int rows_x, int cols_k,
+                          float *dst, int ldp, int sms, cudaStream_t stream);
+
 // Provides [counters | 2*grid slots] for a stream-K launch on `stream`.
 // The handle workspace is grow-only and allocated stream-ordered; false when
 // it cannot be provided (the caller then schedules whole tiles only).

@@ -131,6 +131,55 @@ def test_paths_tails_alignment(cuda, handle, ta, tb, m, n, k, pad, offs):
         _assert(check_full(case, a, b, c, out), (ta, tb, m, n, k, pad, offs, alpha, beta))
 
 
+# Without a workspace (sgblasSgemmNoAlloc) an operand TMA cannot read is
+# staged by the tile kernel's cp.async producer in 4-, 8- or 16-byte copies
+# instead of being copied into the workspace first: cover those paths too.
+COPY_CASES = []
+for ta in (0, 1):
+    for tb in (0, 1):
+        for (m, n, k) in ((300, 200, 70), (257, 129, 33), (5, 300, 17)):
+            for pad, offs in ((1, (0, 0, 0)), (2, (0, 0, 0)), (0, (1, 2, 3)), (4, (2, 0, 1))):
+                COPY_CASES.append((ta, tb, m, n, k, pad, offs))
+
+
+@pytest.mark.parametrize("ta,tb,m,n,k,pad,offs", COPY_CASES)
+def test_copy_staging_without_workspace(cuda, handle, ta, tb, m, n, k, pad, offs):
+    import ctypes
+    torch = cuda
+    lda = (k if ta else m) + pad
+    ldb = (n if tb else k) + pad
+    ldc = m + (pad or 1)
+    f = ctypes.c_float
+    for alpha, beta in ((1.0, 0.0), (0.75, -1.25)):
+        case = C.Case("copy", ta, tb, m, n, k, lda, ldb, ldc, alpha, beta)
+        a, b, c = C.cfg_inputs(case, 300 + m + n + k, None)
+        C.pad_and_poison(c, m, n, ldc, beta, C.PRODUCT_PAD)
+        da, pa = to_device(torch, a, offs[0])
+        db, pb = to_device(torch, b, offs[1])
+        dc, pc = to_device(torch, c, offs[2])
+        status = sg.lib.sgblasSgemmNoAlloc(handle.raw, ta, tb, m, n, k, ctypes.byref(f(alpha)), pa,
+                                           lda, pb, ldb, ctypes.byref(f(beta)), pc, ldc)
+        torch.cuda.synchronize()
+        assert status == 0
+        out = dc[offs[2]:].cpu().numpy()
+        _assert(check_full(case, a, b, c, out), (ta, tb, m, n, k, pad, offs, alpha, beta))
+    assert sg.get_device_errors() == 0
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("pad", [1, 2, 3])
+def test_packed_operands_large(cuda, handle, ta, tb, pad):
+    # Odd or 8-byte leading dimensions on a multi-tile problem: both operands
+    # go through the workspace copies (transposing the k-contiguous ones).
+    m, n, k = 1023, 1537, 777
+    case = C.Case("packed", ta, tb, m, n, k, (k if ta else m) + pad, (n if tb else k) + pad,
+                  m + pad, 1.5, -0.5)
+    a, b, c = C.cfg_inputs(case, 900 + pad, None)
+    status, out = run_sgemm(cuda, handle, case, a, b, c)
+    assert status == 0
+    _assert(check_full(case, a, b, c, out), (ta, tb, pad))
+
+
 def test_deterministic(cuda, handle):
     case = C.cfg3(0, 0)
     a, b, c = C.cfg_inputs(case, 3, None, normal=True)
