@@ -122,6 +122,20 @@ __device__ __forceinline__ void prefetchTensorMap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream is still
+// running; gridDependencyWait blocks until that kernel has completed and its
+// memory operations are visible, so it must precede every global memory
+// access. allowDependentLaunch lets the next kernel in the stream begin its
+// own launch (it still waits in gridDependencyWait for this one to finish).
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void gridDependencyWait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void allowDependentLaunch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Asynchronous prefetch of [ptr, ptr + bytes) from global memory into L2.
 // ptr 16-byte aligned, bytes a non-zero multiple of 16; the range must lie
 // inside one allocation.

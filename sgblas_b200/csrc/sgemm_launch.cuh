@@ -69,6 +69,11 @@ sgblasStatus_t launchTiles(kern::GemmParams p, const Scratch &scratch, int devic
   cfg.blockDim = dim3(kern::kBlockThreads);
   cfg.dynamicSmemBytes = G::kSmemBytes;
   cfg.stream = stream;
+  cudaLaunchAttribute attr[1] = {};
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   const sgblasStatus_t st = launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));
   if (st == SGBLAS_STATUS_SUCCESS && used_handle_workspace &&
       !markWorkspaceUse(scratch.ctx, stream))

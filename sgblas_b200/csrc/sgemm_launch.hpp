@@ -37,7 +37,7 @@ int smCount(int device);
 struct Schedule {
   int grid = 0, dp_tiles = 0, sk_tiles = 0, sk_q = 0, sk_r = 0;
 };
-constexpr int kMinSkIters = 8;
+constexpr int kMinSkIters = 4;
 Schedule makeSchedule(long long tiles, int kiters, int sms);
 
 // Scratch layout: [arrival counters (kCounterRegionBytes) | partial slots].

@@ -7,6 +7,7 @@
 // once) and replaces the tile kernel's 4- or 8-byte cp.async staging, which
 // saturates the producer warpgroup, and any in-kernel transposition of that
 // operand.
+#include "ptx.cuh"
 #include "sgemm_launch.hpp"
 
 #include <cuda_runtime.h>
@@ -27,6 +28,8 @@ __global__ __launch_bounds__(kPackThreads) void packColumnsKernel(const float *_
                                                                  int ld, int rows_x, int cols_k,
                                                                  float *__restrict__ dst, int ldp,
                                                                  int tiles_x, long long tiles) {
+  kern::gridDependencyWait();
+  kern::allowDependentLaunch();
   for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int k = static_cast<int>(t / tiles_x);
     const int x = static_cast<int>(t % tiles_x) * (4 * kPackThreads) + 4 * threadIdx.x;
@@ -54,6 +57,8 @@ __global__ __launch_bounds__(kPackThreads) void packTransposeKernel(const float 
                                                                    long long tiles) {
   __shared__ float tile[kTile][kTile + 1];
   const int lane = threadIdx.x % 32, row = threadIdx.x / 32;
+  kern::gridDependencyWait();
+  kern::allowDependentLaunch();
   for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int x0 = static_cast<int>(t % tiles_x) * kTile;
     const int k0 = static_cast<int>(t / tiles_x) * kTile;
@@ -91,8 +96,16 @@ sgblasStatus_t launchPack(const float *src, int ld, bool k_contiguous, int rows_
   // Eight resident 256-thread blocks per SM cover the latency of the loads.
   const long long grid = std::min<long long>(tiles, static_cast<long long>(sms) * 8);
   void *args[] = {&src, &ld, &rows_x, &cols_k, &dst, &ldp, &tiles_x, &tiles};
-  return launchStatus(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(grid)),
-                                       dim3(kPackThreads), args, 0, stream));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kPackThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1] = {};
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return launchStatus(cudaLaunchKernelExC(&cfg, kernel, args));
 }
 
 }  // namespace sgblas::detail

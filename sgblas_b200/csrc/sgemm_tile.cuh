@@ -409,6 +409,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     fenceBarrierInit();
   }
   __syncthreads();
+  // Launched with programmatic stream serialization: the set-up above may
+  // overlap the previous kernel in the stream; nothing below runs before it
+  // has finished.
+  gridDependencyWait();
+  allowDependentLaunch();
 
   // ======================= producer warpgroup ===============================
   if (tid >= kThreads) {
