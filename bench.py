@@ -55,6 +55,13 @@ def parse_args():
     ap.add_argument("--shape", type=str, default=None,
                     help="N=1 M,N,K (default: --size cubed); e.g. 8192,8192,256 for config 4")
     ap.add_argument("--beta", type=float, default=0.0, help="N=1 beta (config 4 uses 1)")
+    ap.add_argument("--alpha", type=float, default=1.0, help="N=1 alpha (config 3 uses 1.5)")
+    ap.add_argument("--op", choices=["NN", "NT", "TN", "TT"], default="NN",
+                    help="N=1 transpose modes of A and B")
+    ap.add_argument("--pad", type=int, default=0,
+                    help="N=1 leading dimensions = stored rows + PAD (config 3 uses 13)")
+    ap.add_argument("--no-flush", action="store_true",
+                    help="N=1: back-to-back calls without the L2 flush (latency of small calls)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
@@ -267,14 +274,20 @@ def run_single(args) -> None:
         m, n, k = (int(v) for v in args.shape.split(","))
     else:
         m = n = k = args.size
-    beta = args.beta
-    lda, ldb, ldc = m, max(k, 1), m   # column-major NN, tight (ldb >= k)
+    beta, alpha = args.beta, args.alpha
+    ta, tb = int(args.op[0] == "T"), int(args.op[1] == "T")
+    # column-major; ld = stored rows + pad (tight by default)
+    lda = (k if ta else m) + args.pad
+    ldb = (n if tb else k) + args.pad
+    ldc = m + args.pad
+    a_cols, b_cols = (m if ta else k), (k if tb else n)
+    plain = (ta, tb, args.pad, alpha) == (0, 0, 0, 1.0)   # the configs' NN layout
     flops = 2.0 * m * n * k
 
     rng = np.random.default_rng(1)
-    ha = rng.uniform(-1.0, 1.0, m * k).astype(np.float32)
-    hb = rng.uniform(-1.0, 1.0, k * n).astype(np.float32)
-    hc = np.random.default_rng(2).uniform(-1.0, 1.0, m * n).astype(np.float32)
+    ha = rng.uniform(-1.0, 1.0, lda * a_cols).astype(np.float32)
+    hb = rng.uniform(-1.0, 1.0, ldb * b_cols).astype(np.float32)
+    hc = np.random.default_rng(2).uniform(-1.0, 1.0, ldc * n).astype(np.float32)
     da = torch.from_numpy(ha).cuda()
     db = torch.from_numpy(hb).cuda()
     dc = torch.from_numpy(hc).cuda()
@@ -285,11 +298,15 @@ def run_single(args) -> None:
     h.set_stream(stream)
 
     def launch():
-        h.sgemm(0, 0, m, n, k, 1.0, da, lda, db, ldb, beta, dc, ldc)
+        h.sgemm(ta, tb, m, n, k, alpha, da, lda, db, ldb, beta, dc, ldc)
+
+    def flush_l2():
+        if not args.no_flush:
+            flush.zero_()
 
     with torch.cuda.stream(stream):
         for _ in range(warmup):
-            flush.zero_()
+            flush_l2()
             launch()
     torch.cuda.synchronize()
 
@@ -299,7 +316,7 @@ def run_single(args) -> None:
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             for i in range(steps):
-                flush.zero_()
+                flush_l2()
                 ev[i][0].record(stream)
                 launch()
                 ev[i][1].record(stream)
@@ -313,7 +330,8 @@ def run_single(args) -> None:
 
     mhz = clocks["sm_mhz"] or 1965.0
     peak = fp32_peak_tflops(sms, mhz)
-    traffic = profile_traffic(f"sgemm_nn_{m}x{n}x{k}.md")  # DRAM bytes per launch (ncu)
+    # DRAM bytes per launch from an ncu capture of this workload
+    traffic = profile_traffic(f"sgemm_nn_{m}x{n}x{k}.md") if plain and not args.no_flush else None
     roofline = {"bound": "fp32_fma", "achieved": value, "peak": peak, "unit": UNIT,
                 "frac": value / peak, "traffic": traffic,
                 "peak_source": f"{sms} SMs x {FP32_LANES_PER_SM} FP32 lanes x 2 x {mhz:.0f} MHz "
@@ -330,13 +348,15 @@ def run_single(args) -> None:
            "scaling": "weak", "vs_baseline": None,
            "vs_published_a100": value / 17.736,
            "dtype": "f32", "data": "synthetic",
-           "config": {"workload": f"sgemm NN {m}x{n}x{k} column-major alpha=1 beta={beta:g}" +
-                                  (" (BASELINE configs[1])" if (m, n, k, beta) == (4096, 4096, 4096, 0.0)
-                                   else ""),
+           "config": {"workload": f"sgemm {args.op} {m}x{n}x{k} column-major alpha={alpha:g} "
+                                  f"beta={beta:g}" + (f" ld=rows+{args.pad}" if args.pad else "") +
+                                  (" (BASELINE configs[1])"
+                                   if plain and (m, n, k, beta) == (4096, 4096, 4096, 0.0) else ""),
                       "m": m, "n": n, "k": k, "lda": lda, "ldb": ldb, "ldc": ldc,
                       "inputs": "uniform[-1,1) float32 (numpy seeds 1: A,B; 2: C)",
-                      "l2": "flushed before every timed step (256 MiB write outside the "
-                            "step's CUDA events)"},
+                      "l2": ("not flushed: back-to-back calls" if args.no_flush else
+                             "flushed before every timed step (256 MiB write outside the "
+                             "step's CUDA events)")},
            "roofline": roofline, "clocks": clocks, "gpu_launches": steps,
            "device": props.name}
 
@@ -346,15 +366,15 @@ def run_single(args) -> None:
             cb.set_stream(stream)
             dc2 = dc.clone()
             for _ in range(warmup):
-                cb.sgemm(0, 0, m, n, k, 1.0, da.data_ptr(), lda, db.data_ptr(), ldb, beta,
+                cb.sgemm(ta, tb, m, n, k, alpha, da.data_ptr(), lda, db.data_ptr(), ldb, beta,
                          dc2.data_ptr(), ldc)
             cev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(steps)]
             with torch.cuda.stream(stream):
                 for i in range(steps):
-                    flush.zero_()
+                    flush_l2()
                     cev[i][0].record(stream)
-                    st = cb.sgemm(0, 0, m, n, k, 1.0, da.data_ptr(), lda, db.data_ptr(), ldb,
+                    st = cb.sgemm(ta, tb, m, n, k, alpha, da.data_ptr(), lda, db.data_ptr(), ldb,
                                   beta, dc2.data_ptr(), ldc)
                     cev[i][1].record(stream)
             torch.cuda.synchronize()
@@ -369,9 +389,9 @@ def run_single(args) -> None:
         except (OSError, AssertionError) as e:
             out["cublas_pedantic"] = {"unavailable": str(e)}
 
-    if not args.no_e2e:
+    if not args.no_e2e and plain:
         out["e2e"] = e2e_single(torch, sg, ha, hb, hc, beta, m, n, k, max(10, steps // 4), warmup)
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and plain:
         out["cpu_baseline"] = cpu_baseline(ha, hb, m, n, k, lda, ldb, args.cpu_seconds)
     h.close()
     emit(json.dumps(out))
