@@ -60,6 +60,8 @@ def parse_args():
                     help="N=1 transpose modes of A and B")
     ap.add_argument("--pad", type=int, default=0,
                     help="N=1 leading dimensions = stored rows + PAD (config 3 uses 13)")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="N=1: matrices per call (sgblasSgemmStridedBatched when > 1)")
     ap.add_argument("--no-flush", action="store_true",
                     help="N=1: back-to-back calls without the L2 flush (latency of small calls)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -173,6 +175,17 @@ class Cublas:
         return self.lib.cublasGemmEx(self.h, ta, tb, m, n, k, ctypes.byref(al), a, 0, lda, b, 0,
                                      ldb, ctypes.byref(be), c, 0, ldc, 69, -1)
 
+    def sgemm_strided_batched(self, ta, tb, m, n, k, alpha, a, lda, sa, b, ldb, sb, beta, c, ldc,
+                              sc, count) -> int:
+        f = self.lib.cublasGemmStridedBatchedEx
+        vp, ip, ll = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+        f.argtypes = [vp, ip, ip, ip, ip, ip, vp, vp, ip, ip, ll, vp, ip, ip, ll, vp, vp, ip, ip,
+                      ll, ip, ip, ip]
+        al = ctypes.c_float(alpha)
+        be = ctypes.c_float(beta)
+        return f(self.h, ta, tb, m, n, k, ctypes.byref(al), a, 0, lda, sa, b, 0, ldb, sb,
+                 ctypes.byref(be), c, 0, ldc, sc, count, 69, -1)
+
 
 def profile_traffic(name: str):
     """DRAM bytes per launch recorded from an ncu capture (profiles/<name>)."""
@@ -281,13 +294,15 @@ def run_single(args) -> None:
     ldb = (n if tb else k) + args.pad
     ldc = m + args.pad
     a_cols, b_cols = (m if ta else k), (k if tb else n)
-    plain = (ta, tb, args.pad, alpha) == (0, 0, 0, 1.0)   # the configs' NN layout
-    flops = 2.0 * m * n * k
+    batch = args.batch
+    plain = (ta, tb, args.pad, alpha, batch) == (0, 0, 0, 1.0, 1)   # the configs' NN layout
+    flops = 2.0 * m * n * k * batch
+    sa, sb, sc = lda * a_cols, ldb * b_cols, ldc * n     # batch strides (elements)
 
     rng = np.random.default_rng(1)
-    ha = rng.uniform(-1.0, 1.0, lda * a_cols).astype(np.float32)
-    hb = rng.uniform(-1.0, 1.0, ldb * b_cols).astype(np.float32)
-    hc = np.random.default_rng(2).uniform(-1.0, 1.0, ldc * n).astype(np.float32)
+    ha = rng.uniform(-1.0, 1.0, sa * batch).astype(np.float32)
+    hb = rng.uniform(-1.0, 1.0, sb * batch).astype(np.float32)
+    hc = np.random.default_rng(2).uniform(-1.0, 1.0, sc * batch).astype(np.float32)
     da = torch.from_numpy(ha).cuda()
     db = torch.from_numpy(hb).cuda()
     dc = torch.from_numpy(hc).cuda()
@@ -298,7 +313,11 @@ def run_single(args) -> None:
     h.set_stream(stream)
 
     def launch():
-        h.sgemm(ta, tb, m, n, k, alpha, da, lda, db, ldb, beta, dc, ldc)
+        if batch == 1:
+            h.sgemm(ta, tb, m, n, k, alpha, da, lda, db, ldb, beta, dc, ldc)
+        else:
+            h.sgemm_strided_batched(ta, tb, m, n, k, alpha, da, lda, sa, db, ldb, sb, beta, dc,
+                                    ldc, sc, batch)
 
     def flush_l2():
         if not args.no_flush:
@@ -339,8 +358,9 @@ def run_single(args) -> None:
                                "MEASURED_PEAKS.json has no FP32 CUDA-core figure",
                 "frac_of_max_clock": value / fp32_peak_tflops(sms, 1965.0),
                 "algorithmic_flops_per_launch": flops,
-                "algorithmic_bytes_per_launch": 4.0 * (m * k + k * n + m * n * (2 if beta else 1)),
-                "hbm_gbs_algorithmic": 4.0 * (m * k + k * n + m * n * (2 if beta else 1)) /
+                "algorithmic_bytes_per_launch":
+                    4.0 * batch * (m * k + k * n + m * n * (2 if beta else 1)),
+                "hbm_gbs_algorithmic": 4.0 * batch * (m * k + k * n + m * n * (2 if beta else 1)) /
                                        (total_s / steps) / 1e9}
 
     out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": steps,
@@ -348,7 +368,8 @@ def run_single(args) -> None:
            "scaling": "weak", "vs_baseline": None,
            "vs_published_a100": value / 17.736,
            "dtype": "f32", "data": "synthetic",
-           "config": {"workload": f"sgemm {args.op} {m}x{n}x{k} column-major alpha={alpha:g} "
+           "config": {"workload": (f"strided batch of {batch} x " if batch > 1 else "") +
+                                  f"sgemm {args.op} {m}x{n}x{k} column-major alpha={alpha:g} "
                                   f"beta={beta:g}" + (f" ld=rows+{args.pad}" if args.pad else "") +
                                   (" (BASELINE configs[1])"
                                    if plain and (m, n, k, beta) == (4096, 4096, 4096, 0.0) else ""),
@@ -365,26 +386,33 @@ def run_single(args) -> None:
             cb = Cublas()
             cb.set_stream(stream)
             dc2 = dc.clone()
+            def cublas_call():
+                if batch == 1:
+                    return cb.sgemm(ta, tb, m, n, k, alpha, da.data_ptr(), lda, db.data_ptr(),
+                                    ldb, beta, dc2.data_ptr(), ldc)
+                return cb.sgemm_strided_batched(ta, tb, m, n, k, alpha, da.data_ptr(), lda, sa,
+                                                db.data_ptr(), ldb, sb, beta, dc2.data_ptr(), ldc,
+                                                sc, batch)
+
             for _ in range(warmup):
-                cb.sgemm(ta, tb, m, n, k, alpha, da.data_ptr(), lda, db.data_ptr(), ldb, beta,
-                         dc2.data_ptr(), ldc)
+                cublas_call()
             cev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(steps)]
             with torch.cuda.stream(stream):
                 for i in range(steps):
                     flush_l2()
                     cev[i][0].record(stream)
-                    st = cb.sgemm(ta, tb, m, n, k, alpha, da.data_ptr(), lda, db.data_ptr(), ldb,
-                                  beta, dc2.data_ptr(), ldc)
+                    st = cublas_call()
                     cev[i][1].record(stream)
             torch.cuda.synchronize()
             assert st == 0
             cval = flops * steps / (sum(s.elapsed_time(e) for s, e in cev) / 1e3) / 1e12
             out["cublas_pedantic"] = {"value": cval, "unit": UNIT, "ratio": value / cval,
                                       "version": cb.version,
-                                      "call": "cublasGemmEx CUDA_R_32F x3, "
-                                              "CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_PEDANTIC_MATH, "
-                                              "NVIDIA_TF32_OVERRIDE=0"}
+                                      "call": ("cublasGemmEx" if batch == 1 else
+                                               "cublasGemmStridedBatchedEx") +
+                                              " CUDA_R_32F x3, CUBLAS_COMPUTE_32F_PEDANTIC, "
+                                              "CUBLAS_PEDANTIC_MATH, NVIDIA_TF32_OVERRIDE=0"}
             del dc2
         except (OSError, AssertionError) as e:
             out["cublas_pedantic"] = {"unavailable": str(e)}

@@ -44,6 +44,36 @@ sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperation_t trans
                                   const float *b, int ldb, const float *beta,
                                   float *c, int ldc);
 
+/* Batched SGEMM: batch_count products C_i = alpha*op(A_i)*op(B_i) + beta*C_i
+ * that share transa/transb, m, n, k, the leading dimensions and the scalars,
+ * in one launch on the handle's stream. Each matrix follows sgblasSgemm's
+ * semantics (beta == 0 never reads C, padding rows stay untouched) and
+ * accuracy bound; the split of k across CTAs, and so the rounding, may differ
+ * from a single sgblasSgemm call on the same matrix. The arguments
+ * are validated as sgblasSgemm validates them, in the same order, and then
+ * batch_count < 0 gives SGBLAS_STATUS_INVALID_VALUE; batch_count == 0, like
+ * m == 0, is a successful no-op. The C matrices must not overlap each other.
+ * No counterpart in the reference API (its design lists batched GEMM as a v1
+ * non-goal, docs/design.md:102); the argument order is cuBLAS's
+ * cublasSgemmStridedBatched / cublasSgemmBatched.
+ *
+ * Strided: matrix i is a + i*stride_a (b, c alike; strides in elements, any
+ * sign; stride_a or stride_b 0 reuses one matrix for every product). */
+sgblasStatus_t sgblasSgemmStridedBatched(sgblasHandle_t handle, sgblasOperation_t transa,
+                                         sgblasOperation_t transb, int m, int n, int k,
+                                         const float *alpha, const float *a, int lda,
+                                         long long stride_a, const float *b, int ldb,
+                                         long long stride_b, const float *beta, float *c,
+                                         int ldc, long long stride_c, int batch_count);
+
+/* Pointer arrays: a_array, b_array and c_array are DEVICE arrays of
+ * batch_count device pointers (read by the kernels, never by the host). */
+sgblasStatus_t sgblasSgemmBatched(sgblasHandle_t handle, sgblasOperation_t transa,
+                                  sgblasOperation_t transb, int m, int n, int k,
+                                  const float *alpha, const float *const a_array[], int lda,
+                                  const float *const b_array[], int ldb, const float *beta,
+                                  float *const c_array[], int ldc, int batch_count);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -58,6 +58,16 @@ _SIGNATURES = {
     "sgblasGetStatusString": (ctypes.c_char_p, [ctypes.c_int]),
     "sgblasGetDeviceErrors": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]),
     "sgblasSelfTestWaitTimeout": (ctypes.c_int, [ctypes.c_uint, ctypes.POINTER(ctypes.c_int)]),
+    "sgblasSgemmStridedBatched": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                 _c_float_p, ctypes.c_void_p, ctypes.c_int,
+                                                 ctypes.c_longlong, ctypes.c_void_p, ctypes.c_int,
+                                                 ctypes.c_longlong, _c_float_p, ctypes.c_void_p,
+                                                 ctypes.c_int, ctypes.c_longlong, ctypes.c_int]),
+    "sgblasSgemmBatched": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_int, _c_float_p, ctypes.c_void_p,
+                                          ctypes.c_int, ctypes.c_void_p, ctypes.c_int, _c_float_p,
+                                          ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
     "sgblasSgemmNoAlloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int, ctypes.c_int, ctypes.c_int, _c_float_p,
                                            ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
@@ -181,6 +191,27 @@ class Handle:
     def sgemm(self, transa, transb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc) -> None:
         _check("sgblasSgemm",
                self.sgemm_status(transa, transb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc))
+
+    def sgemm_strided_batched_status(self, transa, transb, m, n, k, alpha, a, lda, stride_a, b,
+                                     ldb, stride_b, beta, c, ldc, stride_c, batch_count) -> int:
+        """Raw sgblasSgemmStridedBatched (strides in elements)."""
+        return lib.sgblasSgemmStridedBatched(self._h, transa, transb, m, n, k, _fp(alpha), _ptr(a),
+                                             lda, stride_a, _ptr(b), ldb, stride_b, _fp(beta),
+                                             _ptr(c), ldc, stride_c, batch_count)
+
+    def sgemm_strided_batched(self, *args) -> None:
+        _check("sgblasSgemmStridedBatched", self.sgemm_strided_batched_status(*args))
+
+    def sgemm_batched_status(self, transa, transb, m, n, k, alpha, a_array, lda, b_array, ldb,
+                             beta, c_array, ldc, batch_count) -> int:
+        """Raw sgblasSgemmBatched: a_array/b_array/c_array are device arrays
+        of device pointers (e.g. int64 torch tensors on the GPU)."""
+        return lib.sgblasSgemmBatched(self._h, transa, transb, m, n, k, _fp(alpha), _ptr(a_array),
+                                      lda, _ptr(b_array), ldb, _fp(beta), _ptr(c_array), ldc,
+                                      batch_count)
+
+    def sgemm_batched(self, *args) -> None:
+        _check("sgblasSgemmBatched", self.sgemm_batched_status(*args))
 
 
 MG_UNIQUE_ID_BYTES = 128

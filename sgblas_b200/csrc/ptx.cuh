@@ -118,6 +118,16 @@ __device__ __forceinline__ void tmaLoad2d(void *dst, const CUtensorMap *map, uin
       : "memory");
 }
 
+// 3-D form: x, y within one matrix, z selects the matrix of a strided batch.
+__device__ __forceinline__ void tmaLoad3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x,
+                                          int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smemAddr(dst)),
+      "l"(map), "r"(smemAddr(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetchTensorMap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }

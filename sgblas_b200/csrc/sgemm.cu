@@ -30,13 +30,18 @@ namespace {
 // C = beta * C (or C = 0 without reading C when beta == 0) for the k == 0 /
 // alpha == 0 case. Reference: scaleKernel, src/sgemm_cuda.cu:64-84.
 // Rows are the fast grid axis so that a warp touches one contiguous column run.
+// Batches run along grid z: matrix i is c + i*stride_c, or c_ptrs[i].
 template <bool kZero>
-__global__ void scaleKernel(int m, int n, float beta, float *c, int ldc) {
-  for (int col = blockIdx.y; col < n; col += gridDim.y) {
-    float *column = c + static_cast<size_t>(col) * ldc;
-    for (int row = blockIdx.x * blockDim.x + threadIdx.x; row < m;
-         row += gridDim.x * blockDim.x) {
-      column[row] = kZero ? 0.0F : beta * column[row];
+__global__ void scaleKernel(int m, int n, float beta, float *c, int ldc, int batch,
+                            long long stride_c, float *const *c_ptrs) {
+  for (int bi = blockIdx.z; bi < batch; bi += gridDim.z) {
+    float *matrix = c_ptrs != nullptr ? c_ptrs[bi] : c + bi * stride_c;
+    for (int col = blockIdx.y; col < n; col += gridDim.y) {
+      float *column = matrix + static_cast<size_t>(col) * ldc;
+      for (int row = blockIdx.x * blockDim.x + threadIdx.x; row < m;
+           row += gridDim.x * blockDim.x) {
+        column[row] = kZero ? 0.0F : beta * column[row];
+      }
     }
   }
 }
@@ -51,17 +56,21 @@ sgblasStatus_t launchStatus(cudaError_t e) {
 
 namespace {
 
-sgblasStatus_t launchScale(int m, int n, float beta, float *c, int ldc, cudaStream_t stream) {
+sgblasStatus_t launchScale(int m, int n, float beta, float *c, int ldc, const Batch &batch,
+                           cudaStream_t stream) {
   const unsigned row_blocks = static_cast<unsigned>((m + 255) / 256);
   const dim3 grid(row_blocks < 1024u ? row_blocks : 1024u,
-                  static_cast<unsigned>(n < 65535 ? n : 65535));
+                  static_cast<unsigned>(n < 65535 ? n : 65535),
+                  static_cast<unsigned>(batch.count < 65535 ? batch.count : 65535));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(256);
   cfg.stream = stream;
-  const cudaError_t e = beta == 0.0F
-                            ? cudaLaunchKernelEx(&cfg, scaleKernel<true>, m, n, beta, c, ldc)
-                            : cudaLaunchKernelEx(&cfg, scaleKernel<false>, m, n, beta, c, ldc);
+  const cudaError_t e =
+      beta == 0.0F ? cudaLaunchKernelEx(&cfg, scaleKernel<true>, m, n, beta, c, ldc, batch.count,
+                                        batch.stride_c, batch.c_ptrs)
+                   : cudaLaunchKernelEx(&cfg, scaleKernel<false>, m, n, beta, c, ldc, batch.count,
+                                        batch.stride_c, batch.c_ptrs);
   return launchStatus(e);
 }
 
@@ -94,15 +103,24 @@ EncodeTiledFn encodeTiled() {
 
 }  // namespace
 
-bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld, int box_rows,
-                  int box_cols, bool swizzle64) {
+bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld, int batch,
+                  long long stride, int box_rows, int box_cols, bool swizzle64) {
   const EncodeTiledFn fn = encodeTiled();
   if (fn == nullptr) return false;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(cols)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * sizeof(float)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_rows), static_cast<cuuint32_t>(box_cols)};
-  const cuuint32_t elem_strides[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides, box,
+  // A single matrix is a batch of one; its (unused) batch stride is the
+  // matrix size rounded up to 16 bytes.
+  const long long stride_bytes = batch == 1
+                                     ? (static_cast<long long>(ld) * cols * 4 + 15) / 16 * 16
+                                     : stride * 4;
+  if (stride_bytes <= 0 || stride_bytes % 16 != 0 || stride_bytes >= (1LL << 40)) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(cols),
+                              static_cast<cuuint64_t>(batch)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * sizeof(float),
+                                 static_cast<cuuint64_t>(stride_bytes)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_rows), static_cast<cuuint32_t>(box_cols),
+                             1};
+  const cuuint32_t elem_strides[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(ptr), dims, strides, box,
             elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
             swizzle64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -222,7 +240,7 @@ namespace {
 sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOperation_t tb,
                              int m, int n, int k, float alpha, const float *a, int lda,
                              const float *b, int ldb, float beta, float *c, int ldc,
-                             cudaStream_t stream) {
+                             const Batch &batch, cudaStream_t stream) {
   int device = -1;
   if (cudaGetDevice(&device) != cudaSuccess) {
     (void)cudaGetLastError();
@@ -244,6 +262,13 @@ sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOpe
   p.alpha = alpha;
   p.beta = beta;
   p.err = err;
+  p.batch = batch.count;
+  p.stride_a = batch.stride_a;
+  p.stride_b = batch.stride_b;
+  p.stride_c = batch.stride_c;
+  p.a_ptrs = batch.a_ptrs;
+  p.b_ptrs = batch.b_ptrs;
+  p.c_ptrs = batch.c_ptrs;
   Scratch scratch;
   scratch.ctx = ctx;
 
@@ -252,9 +277,10 @@ sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOpe
   // a multiple of 4 floats) is copied into the workspace as an x-contiguous
   // matrix (A: m x k, as for op N; B: n x k, as for op T) with an aligned
   // leading dimension, and the product runs on TMA staging. Without a
-  // workspace the tile kernel stages it with cp.async instead.
-  const bool pack_a = !(aligned16(a) && lda % 4 == 0);
-  const bool pack_b = !(aligned16(b) && ldb % 4 == 0);
+  // workspace, and for batches, the tile kernel stages it with cp.async.
+  const bool single = batch.count == 1 && batch.a_ptrs == nullptr;
+  const bool pack_a = single && !(aligned16(a) && lda % 4 == 0);
+  const bool pack_b = single && !(aligned16(b) && ldb % 4 == 0);
   bool packed = false;
   if (pack_a || pack_b) {
     const int sms = smCount(device);
@@ -333,7 +359,66 @@ extern "C" sgblasStatus_t sgblasSgemm(sgblasHandle_t handle, sgblasOperation_t t
   if (plan.work == Work::kNothing) return SGBLAS_STATUS_SUCCESS;
   if (handle->math_mode != SGBLAS_MATH_FP32) return SGBLAS_STATUS_NOT_SUPPORTED;
   const auto stream = static_cast<cudaStream_t>(handle->stream);
-  if (plan.work == Work::kScale) return launchScale(m, n, plan.beta, c, ldc, stream);
+  const Batch one;
+  if (plan.work == Work::kScale) return launchScale(m, n, plan.beta, c, ldc, one, stream);
   return launchProduct(handle, transa, transb, m, n, k, plan.alpha, a, lda, b, ldb, plan.beta, c,
-                       ldc, stream);
+                       ldc, one, stream);
+}
+
+// Batched forms (no counterpart in the reference, whose v1 design lists
+// batched GEMM as a non-goal): every matrix of the batch is validated and
+// computed exactly as sgblasSgemm would, in one launch. The pointers checked
+// for NULL are the base pointers (strided) or the device pointer arrays.
+namespace {
+
+sgblasStatus_t sgemmBatch(sgblasHandle_t handle, sgblasOperation_t transa,
+                          sgblasOperation_t transb, int m, int n, int k, const float *alpha,
+                          const float *a, int lda, const float *b, int ldb, const float *beta,
+                          float *c, int ldc, const sgblas::detail::Batch &batch) {
+  using namespace sgblas::detail;
+  if (handle == nullptr) return SGBLAS_STATUS_NOT_INITIALIZED;
+  SgemmPlan plan;
+  const sgblasStatus_t status =
+      validate(transa, transb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc, &plan);
+  if (status != SGBLAS_STATUS_SUCCESS) return status;
+  if (batch.count < 0) return SGBLAS_STATUS_INVALID_VALUE;
+  if (plan.work == Work::kNothing || batch.count == 0) return SGBLAS_STATUS_SUCCESS;
+  if (handle->math_mode != SGBLAS_MATH_FP32) return SGBLAS_STATUS_NOT_SUPPORTED;
+  const auto stream = static_cast<cudaStream_t>(handle->stream);
+  if (plan.work == Work::kScale) return launchScale(m, n, plan.beta, c, ldc, batch, stream);
+  return launchProduct(handle, transa, transb, m, n, k, plan.alpha, a, lda, b, ldb, plan.beta, c,
+                       ldc, batch, stream);
+}
+
+}  // namespace
+
+extern "C" sgblasStatus_t sgblasSgemmStridedBatched(
+    sgblasHandle_t handle, sgblasOperation_t transa, sgblasOperation_t transb, int m, int n,
+    int k, const float *alpha, const float *a, int lda, long long stride_a, const float *b,
+    int ldb, long long stride_b, const float *beta, float *c, int ldc, long long stride_c,
+    int batch_count) {
+  sgblas::detail::Batch batch;
+  batch.count = batch_count;
+  batch.stride_a = stride_a;
+  batch.stride_b = stride_b;
+  batch.stride_c = stride_c;
+  return sgemmBatch(handle, transa, transb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc, batch);
+}
+
+extern "C" sgblasStatus_t sgblasSgemmBatched(sgblasHandle_t handle, sgblasOperation_t transa,
+                                             sgblasOperation_t transb, int m, int n, int k,
+                                             const float *alpha, const float *const a_array[],
+                                             int lda, const float *const b_array[], int ldb,
+                                             const float *beta, float *const c_array[], int ldc,
+                                             int batch_count) {
+  sgblas::detail::Batch batch;
+  batch.count = batch_count;
+  batch.a_ptrs = a_array;
+  batch.b_ptrs = b_array;
+  batch.c_ptrs = c_array;
+  // validate() checks the arrays for NULL where sgblasSgemm checks matrices.
+  return sgemmBatch(handle, transa, transb, m, n, k, alpha,
+                    reinterpret_cast<const float *>(a_array), lda,
+                    reinterpret_cast<const float *>(b_array), ldb, beta,
+                    reinterpret_cast<float *>(const_cast<float **>(c_array)), ldc, batch);
 }

@@ -27,7 +27,7 @@ sgblasStatus_t launchTiles(kern::GemmParams p, const Scratch &scratch, int devic
   p.tiles_n = (p.n + Plan::kBN - 1) / Plan::kBN;
   p.group_m = 8;
   p.kiters = (p.k + kern::kBK - 1) / kern::kBK;
-  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n * p.batch;
   if (tiles > INT_MAX / 2 || static_cast<long long>(p.kiters) * tiles > INT_MAX)
     return SGBLAS_STATUS_NOT_SUPPORTED;
   const int sms = smCount(device);
@@ -101,25 +101,30 @@ sgblasStatus_t launchOriented(kern::GemmParams p, const Scratch &scratch, int de
                               cudaStream_t stream) {
   using Plan = kern::Plan<kTA, kTB, kPairIsA, kTP>;
   using kern::Layout;
-  if (aligned16(p.a) && aligned16(p.b) && p.lda % 4 == 0 && p.ldb % 4 == 0) {
+  const bool arrays = p.a_ptrs != nullptr;   // pointer arrays: no tensor maps
+  auto strideOk = [&](long long stride, int q) { return p.batch == 1 || stride % q == 0; };
+  if (!arrays && aligned16(p.a) && aligned16(p.b) && p.lda % 4 == 0 && p.ldb % 4 == 0 &&
+      strideOk(p.stride_a, 4) && strideOk(p.stride_b, 4)) {
     const bool a_kx = Plan::kA == Layout::kKX;
     const bool b_kx = Plan::kB == Layout::kKX;
     const int bk = kern::kBK;
-    if (encodeMatrix(&p.tma_a, p.a, kTA ? p.k : p.m, kTA ? p.m : p.k, p.lda,
-                     a_kx ? bk : Plan::kAExt, a_kx ? Plan::kAExt : bk, a_kx) &&
-        encodeMatrix(&p.tma_b, p.b, kTB ? p.n : p.k, kTB ? p.k : p.n, p.ldb,
-                     b_kx ? bk : Plan::kBExt, b_kx ? Plan::kBExt : bk, b_kx))
+    if (encodeMatrix(&p.tma_a, p.a, kTA ? p.k : p.m, kTA ? p.m : p.k, p.lda, p.batch,
+                     p.stride_a, a_kx ? bk : Plan::kAExt, a_kx ? Plan::kAExt : bk, a_kx) &&
+        encodeMatrix(&p.tma_b, p.b, kTB ? p.n : p.k, kTB ? p.k : p.n, p.ldb, p.batch,
+                     p.stride_b, b_kx ? bk : Plan::kBExt, b_kx ? Plan::kBExt : bk, b_kx))
       return launchByBeta<kTP, kTA, kTB, kPairIsA, kern::Src::kTma>(p, scratch, device, stream);
   }
-  // Widest cp.async the operand's alignment allows.
-  auto vec = [](const float *ptr, int ld) {
+  // Widest cp.async the operand's alignment allows (for every matrix of a
+  // strided batch; 4 bytes for pointer arrays, whose entries are unknown here).
+  auto vec = [&](const float *ptr, int ld, long long stride) {
+    if (arrays) return 1;
     const uintptr_t addr = reinterpret_cast<uintptr_t>(ptr);
-    if (addr % 16 == 0 && ld % 4 == 0) return 4;
-    if (addr % 8 == 0 && ld % 2 == 0) return 2;
+    if (addr % 16 == 0 && ld % 4 == 0 && strideOk(stride, 4)) return 4;
+    if (addr % 8 == 0 && ld % 2 == 0 && strideOk(stride, 2)) return 2;
     return 1;
   };
-  p.a_vec = vec(p.a, p.lda);
-  p.b_vec = vec(p.b, p.ldb);
+  p.a_vec = vec(p.a, p.lda, p.stride_a);
+  p.b_vec = vec(p.b, p.ldb, p.stride_b);
   return launchByBeta<kTP, kTA, kTB, kPairIsA, kern::Src::kCopy>(p, scratch, device, stream);
 }
 
@@ -148,7 +153,7 @@ template <bool kTA, bool kTB>
 sgblasStatus_t launchMode(kern::GemmParams p, const Scratch &scratch, int device,
                           cudaStream_t stream) {
   auto tiles = [&](long long bm, long long bn) {
-    return ((p.m + bm - 1) / bm) * ((p.n + bn - 1) / bn);
+    return ((p.m + bm - 1) / bm) * ((p.n + bn - 1) / bn) * p.batch;
   };
   const long long large = std::min(tiles(256, 128), tiles(128, 256));
   if (large >= smCount(device)) return launchSized<16, kTA, kTB>(p, scratch, device, stream);

@@ -19,11 +19,12 @@ namespace sgblas::detail {
 
 sgblasStatus_t launchStatus(cudaError_t e);
 
-// Tensor map of a column-major rows x cols FP32 matrix (leading dimension ld)
-// read in boxes of box_rows x box_cols; swizzle64 for k-contiguous tiles whose
-// rows are exactly 64 bytes. False if the driver refuses it.
-bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld, int box_rows,
-                  int box_cols, bool swizzle64);
+// 3-D tensor map of `batch` column-major rows x cols FP32 matrices (leading
+// dimension ld, matrix i at ptr + i*stride floats) read in boxes of
+// box_rows x box_cols of one matrix; swizzle64 for k-contiguous tiles whose
+// rows are exactly 64 bytes. False if the stride or the driver refuses it.
+bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld, int batch,
+                  long long stride, int box_rows, int box_cols, bool swizzle64);
 
 bool aligned16(const void *p);
 
@@ -47,6 +48,17 @@ Schedule makeSchedule(long long tiles, int kiters, int sms);
 // overlapped by another launch's slots).
 constexpr size_t kSlotBytes = kern::Geo<16>::kSlotBytes;  // the largest slot (128 KiB)
 constexpr size_t kCounterRegionBytes = 4096;
+
+// A batch of products sharing sizes, leading dimensions and scalars: matrix
+// i is A + i*stride_a (B, C alike), or a_ptrs[i] etc. when the caller passed
+// device arrays of pointers. One matrix: count 1, no arrays.
+struct Batch {
+  int count = 1;
+  long long stride_a = 0, stride_b = 0, stride_c = 0;
+  const float *const *a_ptrs = nullptr;
+  const float *const *b_ptrs = nullptr;
+  float *const *c_ptrs = nullptr;
+};
 
 // Where a launch takes its stream-K scratch from.
 struct Scratch {

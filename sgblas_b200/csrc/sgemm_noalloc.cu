@@ -108,6 +108,7 @@ extern "C" sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperat
   p.alpha = plan.alpha;
   p.beta = plan.beta;
   p.err = err;
+  p.batch = 1;
   const auto stream = static_cast<cudaStream_t>(handle->stream);
   Scratch fixed;
   fixed.fixed = scratch;

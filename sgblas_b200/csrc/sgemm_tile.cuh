@@ -100,11 +100,18 @@ enum class Src { kTma, kCopy };
 enum class Layout { kXK, kKX };
 
 struct GemmParams {
-  CUtensorMap tma_a;  // valid when the kernel stages tiles with TMA
+  CUtensorMap tma_a;  // valid when the kernel stages tiles with TMA (3-D: x, k, batch)
   CUtensorMap tma_b;
   const float *a;
   const float *b;
   float *c;
+  // Batches: matrix i is A + i*stride_a (B, C alike), or a_ptrs[i] when the
+  // caller passed device arrays of pointers (then a/b/c are unused).
+  int batch;
+  long long stride_a, stride_b, stride_c;
+  const float *const *a_ptrs;
+  const float *const *b_ptrs;
+  float *const *c_ptrs;
   int m, n, k;
   int lda, ldb, ldc;
   float alpha, beta;
@@ -374,11 +381,23 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   };
   auto stageA = [&](int s) { return P::kPairIsA ? stageP(s) : stageD(s); };
   auto stageB = [&](int s) { return P::kPairIsA ? stageD(s) : stageP(s); };
-  auto origin = [&](int tile, int *m0, int *n0) {
+  // Tiles are numbered batch-major; within a matrix they follow rasterTile.
+  const int tiles_per_matrix = p.tiles_m * p.tiles_n;
+  auto origin = [&](int tile, int *m0, int *n0, int *bi) {
     int tm, tn;
-    rasterTile(p, tile, &tm, &tn);
+    *bi = tile / tiles_per_matrix;
+    rasterTile(p, tile - *bi * tiles_per_matrix, &tm, &tn);
     *m0 = tm * P::kBM;
     *n0 = tn * P::kBN;
+  };
+  auto matrixA = [&](int bi) {
+    return p.a_ptrs != nullptr ? p.a_ptrs[bi] : p.a + bi * p.stride_a;
+  };
+  auto matrixB = [&](int bi) {
+    return p.b_ptrs != nullptr ? p.b_ptrs[bi] : p.b + bi * p.stride_b;
+  };
+  auto matrixC = [&](int bi) {
+    return p.c_ptrs != nullptr ? p.c_ptrs[bi] : p.c + bi * p.stride_c;
   };
 
   const int cta = blockIdx.x;
@@ -427,15 +446,16 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     // producer prefetches that block into L2 when it starts loading the tile,
     // a whole tile's main loop before the read: one column per thread, the
     // 16-byte aligned interior of the in-range rows (never outside C).
-    auto prefetchC = [&](const Item &it, int tm0, int tn0) {
+    auto prefetchC = [&](const Item &it, int tm0, int tn0, int bi) {
       if constexpr (kBeta != Beta::kZero) {
         if (it.kb != 0 || it.ke != p.kiters) return;
         const int r1 = min(tm0 + P::kBM, p.m);
+        const float *cbase = matrixC(bi);
 #pragma unroll 1
         for (int cc = pt; cc < P::kBN; cc += kProducerThreads) {
           const int col = tn0 + cc;
           if (col >= p.n) break;
-          const float *colp = p.c + static_cast<size_t>(col) * p.ldc;
+          const float *colp = cbase + static_cast<size_t>(col) * p.ldc;
           const uintptr_t lo = (reinterpret_cast<uintptr_t>(colp + tm0) + 15) & ~uintptr_t{15};
           const uintptr_t hi = reinterpret_cast<uintptr_t>(colp + r1) & ~uintptr_t{15};
           if (hi > lo)
@@ -443,14 +463,19 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         }
       }
     };
-    int idx = 0, kt, ke, m0, n0;
-    {
-      const Item it = itemAt(p, cta, 0);
+    int idx = 0, kt, ke, m0, n0, bi;
+    const float *a_src = nullptr, *b_src = nullptr;  // cp.async: this item's matrices
+    auto startItem = [&](const Item &it) {
       kt = it.kb;
       ke = it.ke;
-      origin(it.tile, &m0, &n0);
-      prefetchC(it, m0, n0);
-    }
+      origin(it.tile, &m0, &n0, &bi);
+      if constexpr (kSrc == Src::kCopy) {
+        a_src = matrixA(bi);
+        b_src = matrixB(bi);
+      }
+      prefetchC(it, m0, n0, bi);
+    };
+    startItem(itemAt(p, cta, 0));
     // Transposes trail the loads by kLag iterations: far enough behind for the
     // data to have landed, early enough to stay up to two iterations ahead of
     // the compute warps. Deadlock-free: the load of iteration i waits for the
@@ -468,26 +493,20 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           if (pt == 0) {
             if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
             mbarArriveExpectTx(&full[s], kStageBytes);
-            if (P::kA == Layout::kXK) tmaLoad2d(stageA(s), &p.tma_a, &full[s], m0, k0);
-            else tmaLoad2d(stageA(s), &p.tma_a, &full[s], k0, m0);
-            if (P::kB == Layout::kXK) tmaLoad2d(stageB(s), &p.tma_b, &full[s], n0, k0);
-            else tmaLoad2d(stageB(s), &p.tma_b, &full[s], k0, n0);
+            if (P::kA == Layout::kXK) tmaLoad3d(stageA(s), &p.tma_a, &full[s], m0, k0, bi);
+            else tmaLoad3d(stageA(s), &p.tma_a, &full[s], k0, m0, bi);
+            if (P::kB == Layout::kXK) tmaLoad3d(stageB(s), &p.tma_b, &full[s], n0, k0, bi);
+            else tmaLoad3d(stageB(s), &p.tma_b, &full[s], k0, n0, bi);
           }
         } else {
           if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
-          copyOperand<P::kAExt, P::kA == Layout::kKX>(p.a, p.lda, p.m, p.k, stageA(s), m0, k0,
+          copyOperand<P::kAExt, P::kA == Layout::kKX>(a_src, p.lda, p.m, p.k, stageA(s), m0, k0,
                                                        pt, p.a_vec);
-          copyOperand<P::kBExt, P::kB == Layout::kKX>(p.b, p.ldb, p.n, p.k, stageB(s), n0, k0,
+          copyOperand<P::kBExt, P::kB == Layout::kKX>(b_src, p.ldb, p.n, p.k, stageB(s), n0, k0,
                                                        pt, p.b_vec);
           cpAsyncArrive(&full[s]);
         }
-        if (++kt == ke && ++idx < nitems) {
-          const Item it = itemAt(p, cta, idx);
-          kt = it.kb;
-          ke = it.ke;
-          origin(it.tile, &m0, &n0);
-          prefetchC(it, m0, n0);
-        }
+        if (++kt == ke && ++idx < nitems) startItem(itemAt(p, cta, idx));
       }
       if constexpr (P::kTrans) {
         const int j = i - kLag;
@@ -524,7 +543,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
 
   const float alpha = p.alpha, beta = p.beta;
-  const bool c_vec = (p.ldc % 4 == 0) && (reinterpret_cast<uintptr_t>(p.c) % 16 == 0);
+  bool c_vec = false;  // float4 access to C: set per tile (batches may differ)
   // C = alpha * acc (+ beta * C) for the tile at (m0, n0). The thread's
   // values come in kGroups groups of four consecutive rows of one column
   // (P = A: four consecutive P coordinates; P = B: four consecutive D
@@ -554,10 +573,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         v[e] = (i & 1) ? acc[i >> 1][4 * h + e].y : acc[i >> 1][4 * h + e].x;
     }
   };
-  auto loadGroup = [&](int row, int col) {
+  auto loadGroup = [&](const float *cbase, int row, int col) {
     float4 cv = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
     if (col >= p.n || row >= p.m) return cv;
-    const float *cp = p.c + static_cast<size_t>(col) * p.ldc + row;
+    const float *cp = cbase + static_cast<size_t>(col) * p.ldc + row;
     if (c_vec && row + 3 < p.m) return *reinterpret_cast<const float4 *>(cp);
     cv.x = cp[0];
     if (row + 1 < p.m) cv.y = cp[1];
@@ -565,9 +584,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     if (row + 3 < p.m) cv.w = cp[3];
     return cv;
   };
-  auto storeGroup = [&](int row, int col, const float v[4], float4 cv) {
+  auto storeGroup = [&](float *cbase, int row, int col, const float v[4], float4 cv) {
     if (col >= p.n || row >= p.m) return;
-    float *cp = p.c + static_cast<size_t>(col) * p.ldc + row;
+    float *cp = cbase + static_cast<size_t>(col) * p.ldc + row;
     float4 out;
     out.x = epilogueValue<kBeta>(v[0], alpha, beta, cv.x);
     out.y = epilogueValue<kBeta>(v[1], alpha, beta, cv.y);
@@ -582,7 +601,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     if (row + 2 < p.m) cp[2] = out.z;
     if (row + 3 < p.m) cp[3] = out.w;
   };
-  auto storeTile = [&](int m0, int n0) {
+  auto storeTile = [&](int m0, int n0, int bi) {
+    float *cbase = matrixC(bi);
+    c_vec = (p.ldc % 4 == 0) && (reinterpret_cast<uintptr_t>(cbase) % 16 == 0);
 #pragma unroll
     for (int g0 = 0; g0 < kGroups; g0 += kBatch) {
       float4 cv[kBatch];
@@ -593,7 +614,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           int row, col;
           float v[4];
           groupAt(g0 + b, m0, n0, &row, &col, v);
-          cv[b] = loadGroup(row, col);
+          cv[b] = loadGroup(cbase, row, col);
         }
       }
 #pragma unroll
@@ -601,7 +622,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         int row, col;
         float v[4];
         groupAt(g0 + b, m0, n0, &row, &col, v);
-        storeGroup(row, col, v, cv[b]);
+        storeGroup(cbase, row, col, v, cv[b]);
       }
     }
   };
@@ -656,10 +677,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
 
     if (++c_kt == c_ke) {
       const Item c_item = itemAt(p, cta, c_idx);
-      int c_m0, c_n0;
-      origin(c_item.tile, &c_m0, &c_n0);
+      int c_m0, c_n0, c_bi;
+      origin(c_item.tile, &c_m0, &c_n0, &c_bi);
       if (c_item.kb == 0 && c_item.ke == p.kiters) {
-        storeTile(c_m0, c_n0);
+        storeTile(c_m0, c_n0, c_bi);
       } else {
         // Stream-K piece: publish, count the arrival, and let the last
         // arriving piece reduce all pieces in piece order.
@@ -679,7 +700,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
 #pragma unroll 1
           for (int c = first; c <= last; ++c) gather(skSlot(p, c, u));
-          storeTile(c_m0, c_n0);
+          storeTile(c_m0, c_n0, c_bi);
           if (tid == 0) p.counters[u] = 0;  // ready for the next launch
         }
       }

@@ -164,3 +164,41 @@ def test_status_strings_match_reference():
     for code in list(range(0, 9)) + [0x7FFFFFFF]:
         assert sg.status_string(code) == ref.dll.refSgblasGetStatusString(code).decode()
     ref.close()
+
+
+# ---- batched entry points: same validation, then the batch count --------------
+@pytest.mark.parametrize("name,args,expected", VALIDATION_CASES, ids=[c[0] for c in VALIDATION_CASES])
+def test_batched_validation_matches_single(handle, name, args, expected):
+    """Every single-matrix validation outcome carries over to both batched
+    forms (strided: base pointers; pointer arrays: the arrays)."""
+    ta, tb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc = args
+    for count in (1, 3):
+        assert handle.sgemm_strided_batched_status(ta, tb, m, n, k, alpha, a, lda, 64, b, ldb, 64,
+                                                   beta, c, ldc, 64, count) == expected
+        assert handle.sgemm_batched_status(ta, tb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc,
+                                           count) == expected
+
+
+def test_batched_count_rules(handle):
+    work = (0, 0, 2, 3, 4, ONE, FAKE_A, 2, FAKE_A, 4, ZERO, FAKE_C, 2)
+    ta, tb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc = work
+    strided = lambda count, **kw: handle.sgemm_strided_batched_status(
+        ta, tb, kw.get("m", m), n, k, alpha, a, kw.get("lda", lda), 8, b, ldb, 12, beta, c, ldc,
+        6, count)
+    arrays = lambda count, **kw: handle.sgemm_batched_status(
+        ta, tb, kw.get("m", m), n, k, alpha, a, kw.get("lda", lda), b, ldb, beta, c, ldc, count)
+    for call in (strided, arrays):
+        assert call(-1) == sg.SGBLAS_STATUS_INVALID_VALUE
+        assert call(0) == sg.SGBLAS_STATUS_SUCCESS              # no work, no device access
+        assert call(-1, m=0) == sg.SGBLAS_STATUS_INVALID_VALUE  # the count is checked after
+        assert call(0, m=0) == sg.SGBLAS_STATUS_SUCCESS         # validation, before quick returns
+        assert call(-1, lda=1) == sg.SGBLAS_STATUS_INVALID_VALUE
+    assert sg.lib.sgblasSgemmStridedBatched(None, 0, 0, 2, 3, 4, None, None, 2, 0, None, 4, 0,
+                                            None, None, 2, 0, 1) == sg.SGBLAS_STATUS_NOT_INITIALIZED
+    assert sg.lib.sgblasSgemmBatched(None, 0, 0, 2, 3, 4, None, None, 2, None, 4, None, None, 2,
+                                     1) == sg.SGBLAS_STATUS_NOT_INITIALIZED
+    handle.set_math_mode(sg.SGBLAS_MATH_TF32)
+    assert strided(2) == sg.SGBLAS_STATUS_NOT_SUPPORTED
+    assert arrays(2) == sg.SGBLAS_STATUS_NOT_SUPPORTED
+    assert strided(0) == sg.SGBLAS_STATUS_SUCCESS
+    handle.set_math_mode(sg.SGBLAS_MATH_FP32)
