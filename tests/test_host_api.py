@@ -202,3 +202,17 @@ def test_batched_count_rules(handle):
     assert arrays(2) == sg.SGBLAS_STATUS_NOT_SUPPORTED
     assert strided(0) == sg.SGBLAS_STATUS_SUCCESS
     handle.set_math_mode(sg.SGBLAS_MATH_FP32)
+
+
+def test_reference_install_consumer_runs_against_product():
+    """The reference's own C consumer (cmake/install-consumer/main.c),
+    compiled unchanged against include/sgblas/sgblas.h and linked to this
+    library by oracle/Makefile, runs to exit status 0 (create, status string,
+    destroy)."""
+    exe = ROOT / "oracle" / "_ref" / "install_consumer_b200"
+    if not exe.exists():
+        pytest.skip("install consumer not built (make -C oracle ref)")
+    libs = subprocess.run(["ldd", str(exe)], capture_output=True, text=True).stdout
+    assert str((ROOT / "sgblas_b200" / "lib" / "libsgblas.so").resolve()) in libs or \
+        "sgblas_b200/lib/libsgblas.so" in libs, libs
+    assert subprocess.run([str(exe)], timeout=60).returncode == 0

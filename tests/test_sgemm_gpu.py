@@ -329,3 +329,28 @@ def test_bounded_wait_times_out_and_reports(cuda):
         status, out = run_sgemm(cuda, h, case, a, b, c)
         assert status == 0
         _assert(check_full(case, a, b, c, out), "after timeout")
+
+
+# ---- the reference's own benchmark, built against this library -----------------
+def test_reference_benchmark_runs_against_product(cuda):
+    """bench/benchmark.cu of the reference, compiled unchanged against this
+    repository's header and libsgblas.so (oracle/Makefile), runs a shape and
+    emits its JSONL evidence schema (metadata + result records)."""
+    import json
+    import pathlib
+    import subprocess
+    exe = pathlib.Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "sgblas_benchmark_b200"
+    if not exe.exists():
+        pytest.skip("reference benchmark not built (make -C oracle ref)")
+    run = subprocess.run([str(exe), "512", "384", "256", "--order", "sgblas-first", "--output",
+                          "jsonl", "--warmups", "2", "--repeats", "5"], capture_output=True,
+                         text=True, timeout=300)
+    assert run.returncode == 0, run.stderr
+    records = [json.loads(line) for line in run.stdout.splitlines() if line.startswith("{")]
+    assert [r["record_type"] for r in records] == ["metadata", "result"]
+    meta, res = records
+    assert meta["schema_version"] == 1
+    assert meta["benchmark"]["sgblas_math_mode"] == "SGBLAS_MATH_FP32"
+    assert meta["device"]["compute_capability_major"] == 10
+    assert (res["m"], res["n"], res["k"]) == (512, 384, 256)
+    assert res["sgblas_gflops"] > 0 and res["cublas_gflops"] > 0 and res["ratio"] > 0
