@@ -36,7 +36,10 @@ import subprocess
 import sys
 import time
 
-os.environ.setdefault("NVIDIA_TF32_OVERRIDE", "0")
+# Strict FP32 everywhere (cuBLAS would otherwise be free to use TF32), except
+# for the TF32 lane (--math tf32), whose comparison is cuBLAS's own TF32 mode.
+if "tf32" not in sys.argv:
+    os.environ.setdefault("NVIDIA_TF32_OVERRIDE", "0")
 
 ROOT = pathlib.Path(__file__).resolve().parent
 METRIC = "strict-FP32 SGEMM TFLOP/s at 4096³ NN vs cuBLAS pedantic and FP32 FMA peak"
@@ -60,6 +63,9 @@ def parse_args():
                     help="N=1 transpose modes of A and B")
     ap.add_argument("--pad", type=int, default=0,
                     help="N=1 leading dimensions = stored rows + PAD (config 3 uses 13)")
+    ap.add_argument("--math", choices=["fp32", "tf32"], default="fp32",
+                    help="N=1: fp32 (the strict default) or the TF32 tensor-core lane "
+                         "(SGBLAS_MATH_TF32; compared with CUBLAS_COMPUTE_32F_FAST_TF32)")
     ap.add_argument("--batch", type=int, default=1,
                     help="N=1: matrices per call (sgblasSgemmStridedBatched when > 1)")
     ap.add_argument("--no-flush", action="store_true",
@@ -146,7 +152,7 @@ def smi_index(torch, dev: int) -> str:
 class Cublas:
     """cublasGemmEx with CUBLAS_COMPUTE_32F_PEDANTIC (comparison lane only)."""
 
-    def __init__(self):
+    def __init__(self, tf32: bool = False):
         self.lib = None
         for name in ("libcublas.so.12", "libcublas.so"):
             try:
@@ -158,7 +164,9 @@ class Cublas:
             raise OSError("libcublas not found")
         self.h = ctypes.c_void_p()
         assert self.lib.cublasCreate_v2(ctypes.byref(self.h)) == 0
-        assert self.lib.cublasSetMathMode(self.h, 2) == 0   # CUBLAS_PEDANTIC_MATH
+        # CUBLAS_PEDANTIC_MATH, or CUBLAS_TF32_TENSOR_OP_MATH for the TF32 lane
+        assert self.lib.cublasSetMathMode(self.h, 3 if tf32 else 2) == 0
+        self.compute = 77 if tf32 else 69   # CUBLAS_COMPUTE_32F_FAST_TF32 / _32F_PEDANTIC
         ver = ctypes.c_int()
         self.lib.cublasGetVersion_v2(self.h, ctypes.byref(ver))
         self.version = ver.value
@@ -173,7 +181,7 @@ class Cublas:
         al = ctypes.c_float(alpha)
         be = ctypes.c_float(beta)
         return self.lib.cublasGemmEx(self.h, ta, tb, m, n, k, ctypes.byref(al), a, 0, lda, b, 0,
-                                     ldb, ctypes.byref(be), c, 0, ldc, 69, -1)
+                                     ldb, ctypes.byref(be), c, 0, ldc, self.compute, -1)
 
     def sgemm_strided_batched(self, ta, tb, m, n, k, alpha, a, lda, sa, b, ldb, sb, beta, c, ldc,
                               sc, count) -> int:
@@ -184,7 +192,7 @@ class Cublas:
         al = ctypes.c_float(alpha)
         be = ctypes.c_float(beta)
         return f(self.h, ta, tb, m, n, k, ctypes.byref(al), a, 0, lda, sa, b, 0, ldb, sb,
-                 ctypes.byref(be), c, 0, ldc, sc, count, 69, -1)
+                 ctypes.byref(be), c, 0, ldc, sc, count, self.compute, -1)
 
 
 def profile_traffic(name: str):
@@ -311,6 +319,10 @@ def run_single(args) -> None:
     stream = torch.cuda.Stream()
     h = sg.Handle()
     h.set_stream(stream)
+    tf32 = args.math == "tf32"
+    if tf32:
+        h.set_math_mode(sg.SGBLAS_MATH_TF32)
+        plain = False
 
     def launch():
         if batch == 1:
@@ -349,14 +361,23 @@ def run_single(args) -> None:
 
     mhz = clocks["sm_mhz"] or 1965.0
     peak = fp32_peak_tflops(sms, mhz)
+    peak_source = (f"{sms} SMs x {FP32_LANES_PER_SM} FP32 lanes x 2 x {mhz:.0f} MHz "
+                   "(median SM clock sampled during the timed region); "
+                   "MEASURED_PEAKS.json has no FP32 CUDA-core figure")
+    if tf32:
+        measured = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+            if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        bf16 = measured.get("bf16_tflops", 1590.0)
+        peak = bf16 / 2.0
+        peak_source = (f"dense TF32 = half the dense BF16 tensor rate; BF16 {bf16:g} TFLOP/s "
+                       + ("measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+                          if "bf16_tflops" in measured else "fallback"))
     # DRAM bytes per launch from an ncu capture of this workload
     traffic = profile_traffic(f"sgemm_nn_{m}x{n}x{k}.md") if plain and not args.no_flush else None
-    roofline = {"bound": "fp32_fma", "achieved": value, "peak": peak, "unit": UNIT,
-                "frac": value / peak, "traffic": traffic,
-                "peak_source": f"{sms} SMs x {FP32_LANES_PER_SM} FP32 lanes x 2 x {mhz:.0f} MHz "
-                               "(median SM clock sampled during the timed region); "
-                               "MEASURED_PEAKS.json has no FP32 CUDA-core figure",
-                "frac_of_max_clock": value / fp32_peak_tflops(sms, 1965.0),
+    roofline = {"bound": "tensor" if tf32 else "fp32_fma", "achieved": value, "peak": peak,
+                "unit": UNIT, "frac": value / peak, "traffic": traffic,
+                "peak_source": peak_source,
+                "frac_of_max_clock": value / (peak if tf32 else fp32_peak_tflops(sms, 1965.0)),
                 "algorithmic_flops_per_launch": flops,
                 "algorithmic_bytes_per_launch":
                     4.0 * batch * (m * k + k * n + m * n * (2 if beta else 1)),
@@ -367,8 +388,9 @@ def run_single(args) -> None:
            "warmup": warmup, "ms_per_step": 1e3 * total_s / steps, "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None,
            "vs_published_a100": value / 17.736,
-           "dtype": "f32", "data": "synthetic",
+           "dtype": "tf32" if tf32 else "f32", "data": "synthetic",
            "config": {"workload": (f"strided batch of {batch} x " if batch > 1 else "") +
+                                  ("TF32 tensor-core " if tf32 else "") +
                                   f"sgemm {args.op} {m}x{n}x{k} column-major alpha={alpha:g} "
                                   f"beta={beta:g}" + (f" ld=rows+{args.pad}" if args.pad else "") +
                                   (" (BASELINE configs[1])"
@@ -383,7 +405,7 @@ def run_single(args) -> None:
 
     if not args.no_cublas:
         try:
-            cb = Cublas()
+            cb = Cublas(tf32=tf32)
             cb.set_stream(stream)
             dc2 = dc.clone()
             def cublas_call():
@@ -407,12 +429,12 @@ def run_single(args) -> None:
             torch.cuda.synchronize()
             assert st == 0
             cval = flops * steps / (sum(s.elapsed_time(e) for s, e in cev) / 1e3) / 1e12
-            out["cublas_pedantic"] = {"value": cval, "unit": UNIT, "ratio": value / cval,
-                                      "version": cb.version,
-                                      "call": ("cublasGemmEx" if batch == 1 else
-                                               "cublasGemmStridedBatchedEx") +
-                                              " CUDA_R_32F x3, CUBLAS_COMPUTE_32F_PEDANTIC, "
-                                              "CUBLAS_PEDANTIC_MATH, NVIDIA_TF32_OVERRIDE=0"}
+            out["cublas_tf32" if tf32 else "cublas_pedantic"] = {
+                "value": cval, "unit": UNIT, "ratio": value / cval, "version": cb.version,
+                "call": ("cublasGemmEx" if batch == 1 else "cublasGemmStridedBatchedEx") +
+                        (" CUDA_R_32F x3, CUBLAS_COMPUTE_32F_FAST_TF32, CUBLAS_TF32_TENSOR_OP_MATH"
+                         if tf32 else " CUDA_R_32F x3, CUBLAS_COMPUTE_32F_PEDANTIC, "
+                                      "CUBLAS_PEDANTIC_MATH, NVIDIA_TF32_OVERRIDE=0")}
             del dc2
         except (OSError, AssertionError) as e:
             out["cublas_pedantic"] = {"unavailable": str(e)}

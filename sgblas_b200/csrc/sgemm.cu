@@ -127,6 +127,20 @@ bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encodeTiled2d(CUtensorMap *map, const float *ptr, unsigned long long dim0,
+                   unsigned long long dim1, unsigned long long stride1_bytes, unsigned box0,
+                   unsigned box1, CUtensorMapSwizzle swizzle) {
+  const EncodeTiledFn fn = encodeTiled();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {dim0, dim1};
+  const cuuint64_t strides[1] = {stride1_bytes};
+  const cuuint32_t box[2] = {box0, box1};
+  const cuuint32_t elem_strides[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides, box,
+            elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---------------------------------------------------------------------------
@@ -314,7 +328,10 @@ sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOpe
     }
   }
   sgblasStatus_t st;
-  if (!tA && !tB) st = launchMode<false, false>(p, scratch, device, stream);
+  if (ctx->math_mode == SGBLAS_MATH_TF32 && single &&
+      tf32Eligible(p.a, p.lda, p.b, p.ldb)) {
+    st = launchTf32(tA, tB, p, device, stream);
+  } else if (!tA && !tB) st = launchMode<false, false>(p, scratch, device, stream);
   else if (!tA && tB) st = launchMode<false, true>(p, scratch, device, stream);
   else if (tA && !tB) st = launchMode<true, false>(p, scratch, device, stream);
   else st = launchMode<true, true>(p, scratch, device, stream);
@@ -357,7 +374,6 @@ extern "C" sgblasStatus_t sgblasSgemm(sgblasHandle_t handle, sgblasOperation_t t
       validate(transa, transb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc, &plan);
   if (status != SGBLAS_STATUS_SUCCESS) return status;
   if (plan.work == Work::kNothing) return SGBLAS_STATUS_SUCCESS;
-  if (handle->math_mode != SGBLAS_MATH_FP32) return SGBLAS_STATUS_NOT_SUPPORTED;
   const auto stream = static_cast<cudaStream_t>(handle->stream);
   const Batch one;
   if (plan.work == Work::kScale) return launchScale(m, n, plan.beta, c, ldc, one, stream);
@@ -383,7 +399,6 @@ sgblasStatus_t sgemmBatch(sgblasHandle_t handle, sgblasOperation_t transa,
   if (status != SGBLAS_STATUS_SUCCESS) return status;
   if (batch.count < 0) return SGBLAS_STATUS_INVALID_VALUE;
   if (plan.work == Work::kNothing || batch.count == 0) return SGBLAS_STATUS_SUCCESS;
-  if (handle->math_mode != SGBLAS_MATH_FP32) return SGBLAS_STATUS_NOT_SUPPORTED;
   const auto stream = static_cast<cudaStream_t>(handle->stream);
   if (plan.work == Work::kScale) return launchScale(m, n, plan.beta, c, ldc, batch, stream);
   return launchProduct(handle, transa, transb, m, n, k, plan.alpha, a, lda, b, ldb, plan.beta, c,

@@ -26,7 +26,23 @@ sgblasStatus_t launchStatus(cudaError_t e);
 bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld, int batch,
                   long long stride, int box_rows, int box_cols, bool swizzle64);
 
+// Plain 2-D tensor map (dim0 contiguous) with the given swizzle.
+bool encodeTiled2d(CUtensorMap *map, const float *ptr, unsigned long long dim0,
+                   unsigned long long dim1, unsigned long long stride1_bytes, unsigned box0,
+                   unsigned box1, CUtensorMapSwizzle swizzle);
+
 bool aligned16(const void *p);
+
+// The TF32 lane (tf32.cu): the tensor-core kernel reads both operands with
+// TMA, so their bases must be 16-byte aligned and their leading dimensions
+// multiples of 4 floats.
+inline bool tf32Eligible(const float *a, int lda, const float *b, int ldb) {
+  return aligned16(a) && aligned16(b) && lda % 4 == 0 && ldb % 4 == 0;
+}
+// One product in TF32 (single matrix; p carries pointers, sizes, scalars and
+// the error word).
+sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, int device,
+                          cudaStream_t stream);
 
 int smCount(int device);
 

@@ -85,7 +85,6 @@ extern "C" sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperat
     // exactly that without allocating.
     return sgblasSgemm(handle, transa, transb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc);
   }
-  if (handle->math_mode != SGBLAS_MATH_FP32) return SGBLAS_STATUS_NOT_SUPPORTED;
   int device = -1;
   if (cudaGetDevice(&device) != cudaSuccess) {
     (void)cudaGetLastError();
@@ -114,6 +113,10 @@ extern "C" sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperat
   fixed.fixed = scratch;
   fixed.fixed_bytes = kScratchBytes;
   const bool tA = transa == SGBLAS_OP_T, tB = transb == SGBLAS_OP_T;
+  // The TF32 lane needs no scratch; operands it cannot read with TMA are
+  // computed in FP32 instead (more accurate than TF32 asks).
+  if (handle->math_mode == SGBLAS_MATH_TF32 && tf32Eligible(a, lda, b, ldb))
+    return launchTf32(tA, tB, p, device, stream);
   if (!tA && !tB) return launchMode<false, false>(p, fixed, device, stream);
   if (!tA && tB) return launchMode<false, true>(p, fixed, device, stream);
   if (tA && !tB) return launchMode<true, false>(p, fixed, device, stream);

@@ -1,0 +1,258 @@
+// The TF32 lane (math mode SGBLAS_MATH_TF32): C = alpha * op(A) * op(B) +
+// beta * C on the 5th-generation tensor cores. Inputs are read as TF32 (the
+// tensor core uses the top 19 bits of each FP32 word: sign, 8-bit exponent,
+// 10-bit mantissa), products are accumulated in FP32 in tensor memory. This
+// is outside the strict-FP32 contract of the default math mode and is only
+// used when the caller selects SGBLAS_MATH_TF32.
+//
+// One persistent CTA per SM walks 128 x 256 tiles of C. Warp roles:
+//   warp 0   TMA producer: 128x32 A and 256x32 B tiles into a 4-stage ring,
+//            128-byte swizzled (16-byte atoms for K-major tiles, 32-byte
+//            atoms for MN-major ones: the canonical UMMA layouts);
+//   warp 1   MMA issuer: per 32-deep k slice, four tcgen05.mma kind::tf32
+//            (M = 128, N = 256, K = 8) into one of two TMEM accumulators;
+//   warp 2   allocates / frees the 512 TMEM columns;
+//   warps 4-7 epilogue: TMEM -> registers (tcgen05.ld, one row of C per
+//            thread) -> alpha/beta -> C, overlapping the next tile's MMAs.
+// Operands may be K-major (k contiguous) or MN-major (m or n contiguous) in
+// global memory; both are staged as TMA writes them and described to the
+// tensor core accordingly, so nothing is transposed.
+//
+// Synchronisation (mbarriers, all waits bounded):
+//   full[s]      stage s loaded (TMA transaction bytes)
+//   empty[s]     the MMAs reading stage s completed (tcgen05.commit)
+//   acc_full[b]  accumulator b holds a finished tile (tcgen05.commit)
+//   acc_empty[b] the 128 epilogue threads have read accumulator b
+#ifndef SGBLAS_B200_TF32_TILE_CUH_
+#define SGBLAS_B200_TF32_TILE_CUH_
+
+#include "ptx.cuh"
+#include "sgemm_tile.cuh"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace sgblas::kern::tf32 {
+
+constexpr int kBM = 128;             // UMMA M
+constexpr int kBN = 256;             // UMMA N
+constexpr int kBK = 32;              // k per stage: one 128-byte swizzle row of FP32
+constexpr int kMmaK = 8;             // k per tcgen05.mma kind::tf32
+constexpr int kStages = 4;
+constexpr int kAccums = 2;           // TMEM accumulators (double buffered)
+constexpr int kTmemColumns = kAccums * kBN;   // 512: all of TMEM
+constexpr int kABytes = kBM * kBK * 4;        // 16 KiB
+constexpr int kBBytes = kBN * kBK * 4;        // 32 KiB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kChunkBytes = 32 * kBK * 4;     // one 32-wide MN chunk of an MN-major tile (4 KiB)
+constexpr int kThreads = 256;
+constexpr int kEpilogueWarp0 = 4;
+constexpr int kBarrierBytes = 8 * (2 * kStages + 2 * kAccums);
+constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+
+struct Tf32Params {
+  CUtensorMap tma_a;   // K-major: (k, m) boxes 32 x 128; MN-major: (m, k) boxes 32 x 32
+  CUtensorMap tma_b;   // K-major: (k, n) boxes 32 x 256; MN-major: (n, k) boxes 32 x 32
+  float *c;
+  int m, n, k, ldc;
+  float alpha, beta;
+  int tiles_m, tiles_n, kiters, group_m;
+  unsigned *err;
+};
+
+// Shared-memory matrix descriptor (tcgen05), version 1.
+// K-major (128-byte swizzle, 16-byte atoms): rows of 128 bytes (32 k), 8-row
+//   groups 1024 bytes apart (SBO); LBO unused.
+// MN-major (128-byte swizzle with 32-byte atoms, the only MN-major layout
+//   TF32 operands support): 128-byte rows of 32 consecutive m (or n) per k,
+//   4-row groups 512 bytes apart (SBO), 32-wide MN chunks kChunkBytes apart
+//   (LBO).
+template <bool kMN>
+__device__ __forceinline__ uint64_t smemDesc(uint32_t addr) {
+  constexpr uint32_t lbo = kMN ? kChunkBytes : 16;
+  constexpr uint32_t sbo = kMN ? 512 : 1024;
+  constexpr uint64_t layout = kMN ? 1 : 2;   // SWIZZLE_128B_BASE32B : SWIZZLE_128B
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
+  d |= static_cast<uint64_t>(1) << 46;   // version
+  d |= layout << 61;
+  return d;
+}
+
+// Instruction descriptor: FP32 accumulator, TF32 A and B, majors, N, M.
+template <bool kAMN, bool kBMN>
+__host__ __device__ constexpr uint32_t instrDesc() {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kAMN) << 15) |
+         (static_cast<uint32_t>(kBMN) << 16) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+         (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+
+template <bool kAMN, bool kBMN, Beta kBeta>
+__global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant__ Tf32Params p) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint32_t tmem_base_slot;
+  unsigned char *smem = smem_raw + ((1024 - (smemAddr(smem_raw) & 1023)) & 1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+  uint64_t *empty = full + kStages;
+  uint64_t *acc_full = empty + kStages;
+  uint64_t *acc_empty = acc_full + kAccums;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  if (my_tiles == 0) return;  // whole CTA, before any barrier
+
+  if (threadIdx.x == 0) {
+    prefetchTensorMap(&p.tma_a);
+    prefetchTensorMap(&p.tma_b);
+    for (int s = 0; s < kStages; ++s) {
+      mbarInit(&full[s], 1);
+      mbarInit(&empty[s], 1);
+    }
+    for (int b = 0; b < kAccums; ++b) {
+      mbarInit(&acc_full[b], 1);
+      mbarInit(&acc_empty[b], 32 * (kThreads / 32 - kEpilogueWarp0));
+    }
+    fenceBarrierInit();
+  }
+  if (warp == 2) {
+    tmemAlloc(&tmem_base_slot, kTmemColumns);
+    tmemRelinquish();
+  }
+  tcgenFenceBefore();
+  __syncthreads();
+  tcgenFenceAfter();
+  const uint32_t tmem_base = tmem_base_slot;
+  gridDependencyWait();
+  allowDependentLaunch();
+
+  auto tileOrigin = [&](int i, int *m0, int *n0) {
+    const int t = blockIdx.x + i * gridDim.x;
+    const int per_group = p.group_m * p.tiles_n;
+    const int group = t / per_group;
+    const int first = group * p.group_m;
+    const int rows = min(p.tiles_m - first, p.group_m);
+    const int in = t - group * per_group;
+    *m0 = (first + in % rows) * kBM;
+    *n0 = (in / rows) * kBN;
+  };
+  bool ok = true;
+  auto wait = [&](uint64_t *bar, int parity) {
+    if (ok) ok = mbarWait(bar, static_cast<uint32_t>(parity), p.err);
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int g = 0;  // k slices issued so far
+      for (int i = 0; i < my_tiles; ++i) {
+        int m0, n0;
+        tileOrigin(i, &m0, &n0);
+        for (int kb = 0; kb < p.kiters; ++kb, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages) wait(&empty[s], (g / kStages - 1) & 1);
+          unsigned char *sa = smem + s * kStageBytes;
+          unsigned char *sb = sa + kABytes;
+          const int k0 = kb * kBK;
+          mbarArriveExpectTx(&full[s], kStageBytes);
+          if constexpr (kAMN) {
+            for (int j = 0; j < kBM / 32; ++j)
+              tmaLoad2d(sa + j * kChunkBytes, &p.tma_a, &full[s], m0 + 32 * j, k0);
+          } else {
+            tmaLoad2d(sa, &p.tma_a, &full[s], k0, m0);
+          }
+          if constexpr (kBMN) {
+            for (int j = 0; j < kBN / 32; ++j)
+              tmaLoad2d(sb + j * kChunkBytes, &p.tma_b, &full[s], n0 + 32 * j, k0);
+          } else {
+            tmaLoad2d(sb, &p.tma_b, &full[s], k0, n0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = instrDesc<kAMN, kBMN>();
+      int g = 0;
+      for (int i = 0; i < my_tiles; ++i) {
+        const int b = i % kAccums;
+        if (i >= kAccums) wait(&acc_empty[b], (i / kAccums - 1) & 1);
+        tcgenFenceAfter();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kBN);
+        for (int kb = 0; kb < p.kiters; ++kb, ++g) {
+          const int s = g % kStages;
+          wait(&full[s], (g / kStages) & 1);
+          tcgenFenceAfter();
+          const uint32_t sa = smemAddr(smem + s * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kMmaK; ++kk) {
+            // K-major: the next 8 k are 32 bytes further along each row;
+            // MN-major: the next 8 k rows are one 1024-byte group further.
+            const uint32_t koff = kAMN ? kk * 1024u : kk * 32u;
+            const uint32_t koff_b = kBMN ? kk * 1024u : kk * 32u;
+            const uint64_t ad = smemDesc<kAMN>(sa + koff);
+            const uint64_t bd = smemDesc<kBMN>(sb + koff_b);
+            mmaTf32(d_tmem, ad, bd, idesc, kb > 0 || kk > 0);
+          }
+          mmaCommit(&empty[s]);  // the stage is free once these MMAs completed
+        }
+        mmaCommit(&acc_full[b]);
+      }
+    }
+  } else if (warp >= kEpilogueWarp0) {
+    // ---------------- epilogue ----------------
+    const int quarter = warp % 4;   // TMEM lanes [32*quarter, 32*quarter + 32)
+    const float alpha = p.alpha, beta = p.beta;
+    for (int i = 0; i < my_tiles; ++i) {
+      const int b = i % kAccums;
+      int m0, n0;
+      tileOrigin(i, &m0, &n0);
+      wait(&acc_full[b], (i / kAccums) & 1);
+      tcgenFenceAfter();
+      const int row = m0 + quarter * 32 + lane;
+      const bool row_ok = row < p.m;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t v[32];
+        tmemLoad32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                       static_cast<uint32_t>(b * kBN + c * 32),
+                   v);
+        const int col0 = n0 + c * 32;
+        float *cp = p.c + static_cast<size_t>(col0) * p.ldc + row;
+        float cv[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          cv[j] = 0.0F;
+          if constexpr (kBeta != Beta::kZero)
+            if (row_ok && col0 + j < p.n) cv[j] = cp[static_cast<size_t>(j) * p.ldc];
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (row_ok && col0 + j < p.n)
+            cp[static_cast<size_t>(j) * p.ldc] =
+                epilogueValue<kBeta>(__uint_as_float(v[j]), alpha, beta, cv[j]);
+        }
+      }
+      tcgenFenceBefore();
+      mbarArrive(&acc_empty[b]);
+    }
+  }
+
+  tcgenFenceBefore();
+  __syncthreads();
+  if (warp == 2) {
+    tcgenFenceAfter();
+    tmemDealloc(tmem_base, kTmemColumns);
+  }
+}
+
+}  // namespace sgblas::kern::tf32
+
+#endif  // SGBLAS_B200_TF32_TILE_CUH_

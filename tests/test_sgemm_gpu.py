@@ -188,17 +188,6 @@ def test_deterministic(cuda, handle):
     assert np.array_equal(out1, out2, equal_nan=True)
 
 
-def test_tf32_mode_rejects_work_on_gpu(cuda, handle):
-    torch = cuda
-    case = C.cfg1()
-    a, b, c = C.cfg_inputs(case, 0, -1)
-    handle.set_math_mode(sg.SGBLAS_MATH_TF32)
-    status, out = run_sgemm(torch, handle, case, a, b, c)
-    assert status == sg.SGBLAS_STATUS_NOT_SUPPORTED
-    assert np.array_equal(out, c)
-    handle.set_math_mode(sg.SGBLAS_MATH_FP32)
-
-
 # ---- parity with the reference library itself ---------------------------------
 def test_parity_with_reference_library(cuda, handle):
     """Both libraries on identical buffers: each within the bound of the FP64

@@ -1,0 +1,150 @@
+"""The TF32 lane (SGBLAS_MATH_TF32) on the GPU: tcgen05 tensor cores.
+
+TF32 mode is outside the strict-FP32 contract (the reference returns
+NOT_SUPPORTED for it, src/sgemm_cuda.cu:719-721; its design lists a TF32 lane
+as future work). The bound used here follows from the format: each input
+keeps 10 explicit mantissa bits (the tensor core reads the top 19 bits of the
+FP32 word), so each product a*b carries a relative error below 2^-9, and the
+FP32 accumulation adds at most (K + 2) roundings:
+
+    |C - C_ref| <= (2^-9 + (K + 2) * 2^-22) * (|alpha| sum|a*b| + |beta*c|)
+
+Beyond the bound, every test keeps sgblasSgemm's other guarantees: beta == 0
+never reads C (NaN poison), padding rows stay untouched, and results are
+reproducible run to run.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+import sgblas_b200 as sg
+from tests import cases as C
+from tests.gpu_util import c_view, run_sgemm, to_device
+
+pytestmark = pytest.mark.gpu
+
+
+def tol_tf32(k, mag):
+    return (2.0 ** -9 + (k + 2) * 2.0 ** -22) * mag
+
+
+def check_tf32(case, a, b, c0, out, what):
+    ref, mag = oracle.sgemm_f64(case.transa, case.transb, case.m, case.n, case.k, case.alpha, a,
+                                case.lda, b, case.ldb, case.beta, c0, case.ldc)
+    got = c_view(out, case.m, case.n, case.ldc).astype(np.float64)
+    assert np.all(np.isfinite(got)), what
+    err = np.abs(got - ref)
+    bound = tol_tf32(case.k, mag)
+    assert np.all(err <= bound), (what, float((err / np.maximum(bound, 1e-30)).max()))
+    pad_in = c0.reshape(case.n, case.ldc)[:, case.m:]
+    pad_out = out.reshape(case.n, case.ldc)[:, case.m:]
+    assert np.array_equal(pad_in, pad_out, equal_nan=True), (what, "padding rows written")
+    return err, mag
+
+
+@pytest.fixture
+def tf32_handle(handle):
+    handle.set_math_mode(sg.SGBLAS_MATH_TF32)
+    yield handle
+    handle.set_math_mode(sg.SGBLAS_MATH_FP32)
+
+
+SHAPES = [(300, 200, 70), (257, 513, 100), (128, 256, 32), (1, 1, 1), (640, 768, 999)]
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_tf32_modes_and_tails(cuda, tf32_handle, ta, tb, m, n, k):
+    for alpha, beta in ((1.0, 0.0), (0.75, -1.25), (1.0, 1.0)):
+        # leading dimensions rounded to 4 floats: the tensor-core kernel reads
+        # the operands in place with TMA
+        lda = -(-(k if ta else m) // 4) * 4 + 4
+        ldb = -(-(n if tb else k) // 4) * 4
+        case = C.Case("tf32", ta, tb, m, n, k, lda, ldb, m + 3, alpha, beta)
+        a, b, c = C.cfg_inputs(case, 700 + m + n + k, None)
+        C.pad_and_poison(c, m, n, case.ldc, beta, C.PRODUCT_PAD)
+        status, out = run_sgemm(cuda, tf32_handle, case, a, b, c)
+        assert status == 0
+        check_tf32(case, a, b, c, out, (ta, tb, m, n, k, alpha, beta))
+    assert sg.get_device_errors() == 0
+
+
+def test_tf32_uses_tensor_cores_and_is_deterministic(cuda, handle):
+    """The TF32 result differs from the strict-FP32 one by TF32-sized errors
+    (so the tensor-core path ran), and repeats bit for bit."""
+    case = C.Case("tf32-vs-fp32", 0, 0, 512, 512, 512, 512, 512, 512, 1.0, 0.0)
+    a, b, c = C.cfg_inputs(case, 5, -1)
+    _, fp32 = run_sgemm(cuda, handle, case, a, b, c)
+    handle.set_math_mode(sg.SGBLAS_MATH_TF32)
+    try:
+        _, t1 = run_sgemm(cuda, handle, case, a, b, c)
+        _, t2 = run_sgemm(cuda, handle, case, a, b, c)
+    finally:
+        handle.set_math_mode(sg.SGBLAS_MATH_FP32)
+    assert np.array_equal(t1, t2)
+    err, mag = check_tf32(case, a, b, c, t1, "tf32")
+    diff = np.abs(t1.astype(np.float64) - fp32)
+    assert diff.max() > 0.0
+    # far above FP32 rounding, within the TF32 bound
+    assert diff.max() > 64 * 2.0 ** -24 * mag.max()
+
+
+@pytest.mark.parametrize("pad,offs", [(1, (0, 0, 0)), (0, (1, 2, 3))])
+def test_tf32_operands_tma_cannot_read(cuda, tf32_handle, pad, offs):
+    """Odd leading dimensions or misaligned bases: the operands are copied
+    into the workspace first, then computed on the tensor cores."""
+    for ta, tb in ((0, 0), (1, 1)):
+        m, n, k = 333, 444, 123
+        case = C.Case("tf32-copy", ta, tb, m, n, k, (k if ta else m) + pad,
+                      (n if tb else k) + pad, m + 1, 1.5, 0.5)
+        a, b, c = C.cfg_inputs(case, 31, None)
+        status, out = run_sgemm(cuda, tf32_handle, case, a, b, c, offsets=offs)
+        assert status == 0
+        check_tf32(case, a, b, c, out, (ta, tb, pad, offs))
+
+
+def test_tf32_large_sampled(cuda, tf32_handle):
+    torch = cuda
+    m = n = k = 4096
+    case = C.Case("tf32-4096", 0, 0, m, n, k, m, k, m, 1.0, 0.0)
+    a, b, c = C.cfg_inputs(case, 1, -1)
+    status, out = run_sgemm(torch, tf32_handle, case, a, b, c)
+    assert status == 0
+    rng = np.random.default_rng(3)
+    rows = np.concatenate([rng.integers(0, m, 2048), np.arange(0, m, 128), np.arange(127, m, 128)])
+    cols = np.concatenate([rng.integers(0, n, 2048), rng.integers(0, n, 2 * (m // 128))])
+    ref, mag = oracle.sgemm_f64_points(0, 0, k, 1.0, a, m, b, k, 0.0, c, m, rows, cols)
+    got = out[rows + cols * m].astype(np.float64)
+    assert np.all(np.abs(got - ref) <= tol_tf32(k, mag))
+    assert np.all(np.isfinite(out))
+
+
+def test_tf32_no_alloc_and_batched(cuda, tf32_handle):
+    """sgblasSgemmNoAlloc runs the TF32 lane without scratch; batched calls
+    in TF32 mode compute in FP32 (within the strict bound, which is tighter)."""
+    torch = cuda
+    case = C.Case("tf32-noalloc", 0, 1, 300, 260, 90, 300, 260, 300, 1.0, 0.0)
+    a, b, c = C.cfg_inputs(case, 9, -1)
+    da, pa = to_device(torch, a)
+    db, pb = to_device(torch, b)
+    dc, pc = to_device(torch, c)
+    f = ctypes.c_float
+    st = sg.lib.sgblasSgemmNoAlloc(tf32_handle.raw, 0, 1, case.m, case.n, case.k,
+                                   ctypes.byref(f(1.0)), pa, case.lda, pb, case.ldb,
+                                   ctypes.byref(f(0.0)), pc, case.ldc)
+    torch.cuda.synchronize()
+    assert st == 0
+    check_tf32(case, a, b, c, dc.cpu().numpy(), "noalloc")
+    dc2, pc2 = to_device(torch, np.concatenate([c, c]))
+    tf32_handle.sgemm_strided_batched(0, 1, case.m, case.n, case.k, 1.0, pa, case.lda, 0, pb,
+                                      case.ldb, 0, 0.0, pc2, case.ldc, case.c_size, 2)
+    torch.cuda.synchronize()
+    ref, mag = oracle.sgemm_f64(0, 1, case.m, case.n, case.k, 1.0, a, case.lda, b, case.ldb, 0.0,
+                                c, case.ldc)
+    both = dc2.cpu().numpy()
+    for i in range(2):
+        got = both[i * case.c_size:(i + 1) * case.c_size]
+        res = oracle.check(c_view(got, case.m, case.n, case.ldc), ref, mag, case.k)
+        assert res["ok_north_star"], (i, res)
