@@ -5,13 +5,14 @@
 // is outside the strict-FP32 contract of the default math mode and is only
 // used when the caller selects SGBLAS_MATH_TF32.
 //
-// One persistent CTA per SM walks 128 x 256 tiles of C. Warp roles:
-//   warp 0   TMA producer: 128x32 A and 256x32 B tiles into a 4-stage ring,
+// One persistent CTA per SM walks 128 x N tiles of C (N = 256, or 128 when
+// that fills the last wave better). Warp roles:
+//   warp 0   TMA producer: 128x32 A and Nx32 B tiles into a stage ring,
 //            128-byte swizzled (16-byte atoms for K-major tiles, 32-byte
 //            atoms for MN-major ones: the canonical UMMA layouts);
 //   warp 1   MMA issuer: per 32-deep k slice, four tcgen05.mma kind::tf32
-//            (M = 128, N = 256, K = 8) into one of two TMEM accumulators;
-//   warp 2   allocates / frees the 512 TMEM columns;
+//            (M = 128, N, K = 8) into one of two TMEM accumulators;
+//   warp 2   allocates / frees the TMEM columns (2 x N);
 //   warps 4-7 epilogue: TMEM -> registers (tcgen05.ld, one row of C per
 //            thread) -> alpha/beta -> C, overlapping the next tile's MMAs.
 // Operands may be K-major (k contiguous) or MN-major (m or n contiguous) in
@@ -37,21 +38,28 @@
 namespace sgblas::kern::tf32 {
 
 constexpr int kBM = 128;             // UMMA M
-constexpr int kBN = 256;             // UMMA N
 constexpr int kBK = 32;              // k per stage: one 128-byte swizzle row of FP32
 constexpr int kMmaK = 8;             // k per tcgen05.mma kind::tf32
-constexpr int kStages = 4;
 constexpr int kAccums = 2;           // TMEM accumulators (double buffered)
-constexpr int kTmemColumns = kAccums * kBN;   // 512: all of TMEM
 constexpr int kABytes = kBM * kBK * 4;        // 16 KiB
-constexpr int kBBytes = kBN * kBK * 4;        // 32 KiB
-constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kChunkBytes = 32 * kBK * 4;     // one 32-wide MN chunk of an MN-major tile (4 KiB)
 constexpr int kThreads = 256;
 constexpr int kEpilogueWarp0 = 4;
-constexpr int kBarrierBytes = 8 * (2 * kStages + 2 * kAccums);
-constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
-static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+
+// Tile width N (UMMA N): 256, or 128 where the 256-wide tiles would leave a
+// poorly filled last wave. The stage ring fills about 192 KiB either way.
+template <int kBN_>
+struct Cfg {
+  static constexpr int kBN = kBN_;
+  static constexpr int kBBytes = kBN * kBK * 4;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = kBN == 256 ? 4 : 6;
+  static constexpr int kTmemColumns = kAccums * kBN;   // 512 or 256
+  static constexpr int kBarrierBytes = 8 * (2 * kStages + 2 * kAccums);
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+  static_assert(kBN == 128 || kBN == 256, "tile width");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+};
 
 struct Tf32Params {
   CUtensorMap tma_a;   // K-major: (k, m) boxes 32 x 128; MN-major: (m, k) boxes 32 x 32
@@ -85,15 +93,19 @@ __device__ __forceinline__ uint64_t smemDesc(uint32_t addr) {
 }
 
 // Instruction descriptor: FP32 accumulator, TF32 A and B, majors, N, M.
-template <bool kAMN, bool kBMN>
+template <int kBN, bool kAMN, bool kBMN>
 __host__ __device__ constexpr uint32_t instrDesc() {
   return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kAMN) << 15) |
          (static_cast<uint32_t>(kBMN) << 16) | (static_cast<uint32_t>(kBN >> 3) << 17) |
          (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 
-template <bool kAMN, bool kBMN, Beta kBeta>
+template <int kBN, bool kAMN, bool kBMN, Beta kBeta>
 __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant__ Tf32Params p) {
+  using G = Cfg<kBN>;
+  constexpr int kStages = G::kStages;
+  constexpr int kStageBytes = G::kStageBytes;
+  constexpr int kTmemColumns = G::kTmemColumns;
   extern __shared__ unsigned char smem_raw[];
   __shared__ uint32_t tmem_base_slot;
   unsigned char *smem = smem_raw + ((1024 - (smemAddr(smem_raw) & 1023)) & 1023);
@@ -178,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = instrDesc<kAMN, kBMN>();
+      constexpr uint32_t idesc = instrDesc<kBN, kAMN, kBMN>();
       int g = 0;
       for (int i = 0; i < my_tiles; ++i) {
         const int b = i % kAccums;

@@ -148,3 +148,22 @@ def test_tf32_no_alloc_and_batched(cuda, tf32_handle):
         got = both[i * case.c_size:(i + 1) * case.c_size]
         res = oracle.check(c_view(got, case.m, case.n, case.ldc), ref, mag, case.k)
         assert res["ok_north_star"], (i, res)
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_tf32_wide_tiles(cuda, tf32_handle, ta, tb):
+    """4736 x 1024: exactly one wave of 256-wide tiles on 148 SMs, so the
+    256-wide kernel runs (small problems take the 128-wide one); sampled."""
+    m, n, k = 4736, 1024, 96
+    lda, ldb = (k if ta else m), (n if tb else k)
+    case = C.Case("tf32-wide", ta, tb, m, n, k, lda, ldb, m, 0.5, 2.0)
+    a, b, c = C.cfg_inputs(case, 17, None)
+    status, out = run_sgemm(cuda, tf32_handle, case, a, b, c)
+    assert status == 0
+    rng = np.random.default_rng(ta * 2 + tb)
+    rows = np.concatenate([rng.integers(0, m, 4096), np.arange(0, m, 128), np.arange(127, m, 128)])
+    cols = np.concatenate([rng.integers(0, n, 4096), rng.integers(0, n, 2 * (m // 128))])
+    ref, mag = oracle.sgemm_f64_points(ta, tb, k, 0.5, a, lda, b, ldb, 2.0, c, m, rows, cols)
+    got = out[rows + cols * m].astype(np.float64)
+    assert np.all(np.abs(got - ref) <= tol_tf32(k, mag))
+    assert np.all(np.isfinite(out))
