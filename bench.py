@@ -373,7 +373,9 @@ def run_single(args) -> None:
                        + ("measured (MEASURED_PEAKS.json bf16_tflops, burst)"
                           if "bf16_tflops" in measured else "fallback"))
     # DRAM bytes per launch from an ncu capture of this workload
-    traffic = profile_traffic(f"sgemm_nn_{m}x{n}x{k}.md") if plain and not args.no_flush else None
+    traffic = None
+    if not args.no_flush and (ta, tb, args.pad, batch, beta) == (0, 0, 0, 1, 0.0):
+        traffic = profile_traffic(("tf32" if tf32 else "sgemm") + f"_nn_{m}x{n}x{k}.md")
     roofline = {"bound": "tensor" if tf32 else "fp32_fma", "achieved": value, "peak": peak,
                 "unit": UNIT, "frac": value / peak, "traffic": traffic,
                 "peak_source": peak_source,
