@@ -89,8 +89,8 @@ __device__ __forceinline__ void cpAsyncArrive(uint64_t *bar) {
                : "memory");
 }
 
-// Named barrier over the first `count` threads of the CTA (id 0 is
-// __syncthreads).
+// Named barrier kId for kCount threads, whole warps (id 0 is the one
+// __syncthreads uses).
 template <int kId, int kCount>
 __device__ __forceinline__ void namedBarrier() {
   asm volatile("bar.sync %0, %1;" ::"n"(kId), "n"(kCount) : "memory");

@@ -330,7 +330,7 @@ sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOpe
   sgblasStatus_t st;
   if (ctx->math_mode == SGBLAS_MATH_TF32 && single &&
       tf32Eligible(p.a, p.lda, p.b, p.ldb)) {
-    st = launchTf32(tA, tB, p, device, stream);
+    st = launchTf32(tA, tB, p, scratch, device, stream);
   } else if (!tA && !tB) st = launchMode<false, false>(p, scratch, device, stream);
   else if (!tA && tB) st = launchMode<false, true>(p, scratch, device, stream);
   else if (tA && !tB) st = launchMode<true, false>(p, scratch, device, stream);

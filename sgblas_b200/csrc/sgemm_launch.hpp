@@ -33,16 +33,7 @@ bool encodeTiled2d(CUtensorMap *map, const float *ptr, unsigned long long dim0,
 
 bool aligned16(const void *p);
 
-// The TF32 lane (tf32.cu): the tensor-core kernel reads both operands with
-// TMA, so their bases must be 16-byte aligned and their leading dimensions
-// multiples of 4 floats.
-inline bool tf32Eligible(const float *a, int lda, const float *b, int ldb) {
-  return aligned16(a) && aligned16(b) && lda % 4 == 0 && ldb % 4 == 0;
-}
-// One product in TF32 (single matrix; p carries pointers, sizes, scalars and
-// the error word).
-sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, int device,
-                          cudaStream_t stream);
+
 
 int smCount(int device);
 
@@ -104,6 +95,17 @@ sgblasStatus_t launchPack(const float *src, int ld, bool k_contiguous, int rows_
 bool ensureWorkspace(sgblasContext *ctx, size_t bytes, int device, cudaStream_t stream);
 // Marks the end of a launch that used the handle workspace.
 bool markWorkspaceUse(sgblasContext *ctx, cudaStream_t stream);
+
+// The TF32 lane (tf32.cu): the tensor-core kernel reads both operands with
+// TMA, so their bases must be 16-byte aligned and their leading dimensions
+// multiples of 4 floats.
+inline bool tf32Eligible(const float *a, int lda, const float *b, int ldb) {
+  return aligned16(a) && aligned16(b) && lda % 4 == 0 && ldb % 4 == 0;
+}
+// One product in TF32 (single matrix; p carries pointers, sizes, scalars and
+// the error word).
+sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, const Scratch &scratch,
+                          int device, cudaStream_t stream);
 
 // Launches one product of transpose mode (kTA, kTB). p carries the problem
 // (pointers, sizes, alpha, beta, error word); the launcher fills in the rest.

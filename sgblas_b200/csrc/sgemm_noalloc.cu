@@ -113,10 +113,11 @@ extern "C" sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperat
   fixed.fixed = scratch;
   fixed.fixed_bytes = kScratchBytes;
   const bool tA = transa == SGBLAS_OP_T, tB = transb == SGBLAS_OP_T;
-  // The TF32 lane needs no scratch; operands it cannot read with TMA are
-  // computed in FP32 instead (more accurate than TF32 asks).
+  // The TF32 lane takes its stream-K scratch from the same fixed array;
+  // operands it cannot read with TMA are computed in FP32 instead (more
+  // accurate than TF32 asks).
   if (handle->math_mode == SGBLAS_MATH_TF32 && tf32Eligible(a, lda, b, ldb))
-    return launchTf32(tA, tB, p, device, stream);
+    return launchTf32(tA, tB, p, fixed, device, stream);
   if (!tA && !tB) return launchMode<false, false>(p, fixed, device, stream);
   if (!tA && tB) return launchMode<false, true>(p, fixed, device, stream);
   if (tA && !tB) return launchMode<true, false>(p, fixed, device, stream);

@@ -139,21 +139,28 @@ struct Item {
   int tile, kb, ke;
 };
 
-__device__ __forceinline__ int skBegin(const GemmParams &p, int c) {
+// Schedule helpers; Sched is any parameter block with the schedule fields of
+// GemmParams (grid, dp_tiles, sk_tiles, sk_q, sk_r, kiters; tiles_m,
+// tiles_n, group_m for the raster).
+template <class Sched>
+__device__ __forceinline__ int skBegin(const Sched &p, int c) {
   return c * p.sk_q + min(c, p.sk_r);
 }
 
 // The CTA owning stream-K iteration x (inverse of skBegin).
-__device__ __forceinline__ int skOwner(const GemmParams &p, int x) {
+template <class Sched>
+__device__ __forceinline__ int skOwner(const Sched &p, int x) {
   const int head = p.sk_r * (p.sk_q + 1);
   return x < head ? x / (p.sk_q + 1) : p.sk_r + (x - head) / p.sk_q;
 }
 
-__device__ __forceinline__ int dpItems(const GemmParams &p, int c) {
+template <class Sched>
+__device__ __forceinline__ int dpItems(const Sched &p, int c) {
   return c < p.dp_tiles ? (p.dp_tiles - 1 - c) / p.grid + 1 : 0;
 }
 
-__device__ __forceinline__ int numItems(const GemmParams &p, int c) {
+template <class Sched>
+__device__ __forceinline__ int numItems(const Sched &p, int c) {
   int n = dpItems(p, c);
   if (p.sk_tiles > 0) {
     const int s = skBegin(p, c), e = skBegin(p, c + 1);
@@ -162,7 +169,8 @@ __device__ __forceinline__ int numItems(const GemmParams &p, int c) {
   return n;
 }
 
-__device__ __forceinline__ Item itemAt(const GemmParams &p, int c, int idx) {
+template <class Sched>
+__device__ __forceinline__ Item itemAt(const Sched &p, int c, int idx) {
   const int ndp = dpItems(p, c);
   if (idx < ndp) return {c + idx * p.grid, 0, p.kiters};
   const int s = skBegin(p, c), e = skBegin(p, c + 1);
@@ -173,7 +181,8 @@ __device__ __forceinline__ Item itemAt(const GemmParams &p, int c, int idx) {
 
 // Workspace slot of CTA c's piece of stream-K tile u: slot 2c holds the piece
 // of the first tile c touches, slot 2c+1 the piece of its last one.
-__device__ __forceinline__ int skSlot(const GemmParams &p, int c, int u) {
+template <class Sched>
+__device__ __forceinline__ int skSlot(const Sched &p, int c, int u) {
   return 2 * c + (u == skBegin(p, c) / p.kiters ? 0 : 1);
 }
 
@@ -204,7 +213,8 @@ struct Plan {
 
 // Tile index -> (tile_m, tile_n): groups of group_m tile rows are walked
 // column by column so that concurrently running CTAs share panels in L2.
-__device__ __forceinline__ void rasterTile(const GemmParams &p, int t, int *tm, int *tn) {
+template <class Sched>
+__device__ __forceinline__ void rasterTile(const Sched &p, int t, int *tm, int *tn) {
   const int per_group = p.group_m * p.tiles_n;
   const int group = t / per_group;
   const int first = group * p.group_m;

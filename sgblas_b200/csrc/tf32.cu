@@ -17,17 +17,87 @@ namespace {
 
 namespace t = kern::tf32;
 
+Schedule makeScheduleTf32(long long tiles, int kiters, int sms) {
+  Schedule s;
+  const int t = static_cast<int>(tiles);
+  const bool splittable = kiters >= 2 * kMinSkIters;
+  if (t >= sms) {
+    const int rem = t % sms;
+    s.grid = sms;
+    if (rem == 0 || 10 * rem >= 7 * sms || !splittable ||
+        static_cast<long long>(rem) * kiters < static_cast<long long>(sms) * kMinSkIters) {
+      s.dp_tiles = t;
+    } else {
+      s.dp_tiles = t - rem;
+      s.sk_tiles = rem;
+    }
+  } else if (2 * t >= sms || !splittable) {
+    s.grid = t;
+    s.dp_tiles = t;
+  } else {
+    s.grid = static_cast<int>(
+        std::min<long long>(sms, std::max<long long>(tiles, tiles * kiters / kMinSkIters)));
+    s.sk_tiles = t;
+  }
+  if (s.sk_tiles > 0) {
+    const long long it = static_cast<long long>(s.sk_tiles) * kiters;
+    s.sk_q = static_cast<int>(it / s.grid);
+    s.sk_r = static_cast<int>(it % s.grid);
+  }
+  return s;
+}
+
 template <int kBN, bool kAMN, bool kBMN, kern::Beta kBeta>
-sgblasStatus_t launchTyped(t::Tf32Params &q, int sms, int device, cudaStream_t stream) {
+sgblasStatus_t launchTyped(t::Tf32Params &q, const Scratch &scratch, int sms, int device,
+                           cudaStream_t stream) {
   using G = t::Cfg<kBN>;
   auto kernel = t::tf32Kernel<kBN, kAMN, kBMN, kBeta>;
   static std::atomic<uint64_t> configured{0};
   if (!configureKernel(reinterpret_cast<const void *>(kernel), device, G::kSmemBytes,
                        &configured))
     return SGBLAS_STATUS_EXECUTION_FAILED;
+  // Persistent schedule with the FP32 kernel's item structure and
+  // workspace layout ([counters | 2 * grid slots of 128 x kBN floats]), but a
+  // tensor-core tile computes about ten times faster than a CUDA-core one,
+  // so the piece fix-up costs relatively more: only a partial last wave that
+  // leaves more than 30 % of the SMs idle is split (over all CTAs, each
+  // taking less than one tile), and a small problem only when it would leave
+  // more than half of them idle.
   const long long tiles = static_cast<long long>(q.tiles_m) * q.tiles_n;
+  Schedule s = makeScheduleTf32(tiles, q.kiters, sms);
+  bool used_handle_workspace = false;
+  if (s.sk_tiles > 0) {
+    static_assert(static_cast<size_t>(t::kBM) * kBN * 4 <= kSlotBytes, "piece slot size");
+    const size_t need = kCounterRegionBytes + 2 * static_cast<size_t>(s.grid) * kSlotBytes;
+    const bool counters_fit = static_cast<size_t>(s.sk_tiles) * sizeof(int) <= kCounterRegionBytes;
+    unsigned char *base = nullptr;
+    if (scratch.fixed != nullptr) {
+      if (counters_fit && need <= scratch.fixed_bytes) {
+        if (cudaMemsetAsync(scratch.fixed, 0, static_cast<size_t>(s.sk_tiles) * sizeof(int),
+                            stream) != cudaSuccess)
+          return launchStatus(cudaErrorUnknown);   // clears the memset's own error
+        base = scratch.fixed;
+      }
+    } else if (counters_fit && ensureWorkspace(scratch.ctx, need, device, stream)) {
+      base = static_cast<unsigned char *>(scratch.ctx->workspace);
+      used_handle_workspace = true;
+    }
+    if (base != nullptr) {
+      q.counters = reinterpret_cast<int *>(base);
+      q.ws = reinterpret_cast<float *>(base + kCounterRegionBytes);
+    } else {  // no scratch: whole tiles only
+      s = Schedule{};
+      s.grid = static_cast<int>(std::min<long long>(tiles, sms));
+      s.dp_tiles = static_cast<int>(tiles);
+    }
+  }
+  q.grid = s.grid;
+  q.dp_tiles = s.dp_tiles;
+  q.sk_tiles = s.sk_tiles;
+  q.sk_q = s.sk_q;
+  q.sk_r = s.sk_r;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(std::min<long long>(tiles, sms)));
+  cfg.gridDim = dim3(static_cast<unsigned>(s.grid));
   cfg.blockDim = dim3(t::kThreads);
   cfg.dynamicSmemBytes = G::kSmemBytes;
   cfg.stream = stream;
@@ -36,20 +106,27 @@ sgblasStatus_t launchTyped(t::Tf32Params &q, int sms, int device, cudaStream_t s
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return launchStatus(cudaLaunchKernelEx(&cfg, kernel, q));
+  const sgblasStatus_t st = launchStatus(cudaLaunchKernelEx(&cfg, kernel, q));
+  if (st == SGBLAS_STATUS_SUCCESS && used_handle_workspace &&
+      !markWorkspaceUse(scratch.ctx, stream))
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  return st;
 }
 
 template <int kBN, bool kAMN, bool kBMN>
-sgblasStatus_t launchByBeta(t::Tf32Params &q, int sms, int device, cudaStream_t stream) {
+sgblasStatus_t launchByBeta(t::Tf32Params &q, const Scratch &scratch, int sms, int device,
+                            cudaStream_t stream) {
   using kern::Beta;
-  if (q.beta == 0.0F) return launchTyped<kBN, kAMN, kBMN, Beta::kZero>(q, sms, device, stream);
-  if (q.beta == 1.0F) return launchTyped<kBN, kAMN, kBMN, Beta::kOne>(q, sms, device, stream);
-  return launchTyped<kBN, kAMN, kBMN, Beta::kGeneral>(q, sms, device, stream);
+  if (q.beta == 0.0F)
+    return launchTyped<kBN, kAMN, kBMN, Beta::kZero>(q, scratch, sms, device, stream);
+  if (q.beta == 1.0F)
+    return launchTyped<kBN, kAMN, kBMN, Beta::kOne>(q, scratch, sms, device, stream);
+  return launchTyped<kBN, kAMN, kBMN, Beta::kGeneral>(q, scratch, sms, device, stream);
 }
 
 template <int kBN>
 sgblasStatus_t launchSized(const kern::GemmParams &p, bool a_mn, bool b_mn, t::Tf32Params &q,
-                           int sms, int device, cudaStream_t stream) {
+                           const Scratch &scratch, int sms, int device, cudaStream_t stream) {
   q.tiles_n = (p.n + kBN - 1) / kBN;
   // K-major tiles: 128-byte swizzle; MN-major tiles: 128-byte swizzle of
   // 32-byte atoms (what the tensor core requires for MN-major TF32).
@@ -62,16 +139,16 @@ sgblasStatus_t launchSized(const kern::GemmParams &p, bool a_mn, bool b_mn, t::T
   const bool ok_b = b_mn ? encodeTiled2d(&q.tma_b, p.b, p.n, p.k, ldb_b, 32, 32, sw_mn)
                          : encodeTiled2d(&q.tma_b, p.b, p.k, p.n, ldb_b, 32, kBN, sw_k);
   if (!ok_a || !ok_b) return SGBLAS_STATUS_EXECUTION_FAILED;
-  if (a_mn && b_mn) return launchByBeta<kBN, true, true>(q, sms, device, stream);
-  if (a_mn) return launchByBeta<kBN, true, false>(q, sms, device, stream);
-  if (b_mn) return launchByBeta<kBN, false, true>(q, sms, device, stream);
-  return launchByBeta<kBN, false, false>(q, sms, device, stream);
+  if (a_mn && b_mn) return launchByBeta<kBN, true, true>(q, scratch, sms, device, stream);
+  if (a_mn) return launchByBeta<kBN, true, false>(q, scratch, sms, device, stream);
+  if (b_mn) return launchByBeta<kBN, false, true>(q, scratch, sms, device, stream);
+  return launchByBeta<kBN, false, false>(q, scratch, sms, device, stream);
 }
 
 }  // namespace
 
-sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, int device,
-                          cudaStream_t stream) {
+sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, const Scratch &scratch,
+                          int device, cudaStream_t stream) {
   t::Tf32Params q = {};
   q.c = p.c;
   q.m = p.m;
@@ -86,10 +163,10 @@ sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, int devic
   q.group_m = 8;
   const int sms = smCount(device);
   if (sms <= 0) return SGBLAS_STATUS_EXECUTION_FAILED;
-  // Tile width: the one with the shorter estimated run, waves x tile time.
-  // A 128-wide tile takes 0.77 of a 256-wide tile's time (measured: its
-  // operand traffic per FLOP is higher), so it wins only where the 256-wide
-  // tiles leave most of a wave idle.
+  // Tile width: 256, whose partial last wave stream-K balances, once there
+  // are at least as many 256-wide tiles as SMs. Below that, the one with the
+  // shorter estimated run, waves x tile time: a 128-wide tile takes 0.77 of a
+  // 256-wide tile's time (measured: its operand traffic per FLOP is higher).
   auto waves = [&](long long bn) {
     const long long tiles = static_cast<long long>(q.tiles_m) * ((p.n + bn - 1) / bn);
     return (tiles + sms - 1) / sms;
@@ -99,9 +176,10 @@ sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, int devic
   // A: op N keeps m contiguous (MN-major), op T keeps k contiguous (K-major);
   // B: op N keeps k contiguous (K-major), op T keeps n contiguous (MN-major).
   const bool a_mn = !ta, b_mn = tb;
-  if (waves(128) * 77 < waves(256) * 100)
-    return launchSized<128>(p, a_mn, b_mn, q, sms, device, stream);
-  return launchSized<256>(p, a_mn, b_mn, q, sms, device, stream);
+  const long long wide_tiles = static_cast<long long>(q.tiles_m) * ((p.n + 255) / 256);
+  if (wide_tiles < sms && waves(128) * 77 < waves(256) * 100)
+    return launchSized<128>(p, a_mn, b_mn, q, scratch, sms, device, stream);
+  return launchSized<256>(p, a_mn, b_mn, q, scratch, sms, device, stream);
 }
 
 }  // namespace sgblas::detail

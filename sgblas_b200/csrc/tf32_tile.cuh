@@ -63,12 +63,18 @@ struct Cfg {
 
 struct Tf32Params {
   CUtensorMap tma_a;   // K-major: (k, m) boxes 32 x 128; MN-major: (m, k) boxes 32 x 32
-  CUtensorMap tma_b;   // K-major: (k, n) boxes 32 x 256; MN-major: (n, k) boxes 32 x 32
+  CUtensorMap tma_b;   // K-major: (k, n) boxes 32 x N; MN-major: (n, k) boxes 32 x 32
   float *c;
   int m, n, k, ldc;
   float alpha, beta;
   int tiles_m, tiles_n, kiters, group_m;
   unsigned *err;
+  // Persistent schedule, as in the FP32 kernel: whole tiles [0, dp_tiles)
+  // round-robin, then tiles [dp_tiles, dp_tiles + sk_tiles) split by k slices
+  // over all CTAs (stream-K), pieces summed in order by the last arriver.
+  int grid, dp_tiles, sk_tiles, sk_q, sk_r;
+  float *ws;          // 2 * grid piece slots of 128 x N floats
+  int *counters;      // sk_tiles arrival counters, zero between launches
 };
 
 // Shared-memory matrix descriptor (tcgen05), version 1.
@@ -114,10 +120,11 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
   uint64_t *acc_full = empty + kStages;
   uint64_t *acc_empty = acc_full + kAccums;
 
+  __shared__ int last_arrival;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int tiles = p.tiles_m * p.tiles_n;
-  const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  if (my_tiles == 0) return;  // whole CTA, before any barrier
+  const int cta = blockIdx.x;
+  const int nitems = numItems(p, cta);
+  if (nitems == 0) return;  // whole CTA, before any barrier
 
   if (threadIdx.x == 0) {
     prefetchTensorMap(&p.tma_a);
@@ -143,15 +150,11 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
   gridDependencyWait();
   allowDependentLaunch();
 
-  auto tileOrigin = [&](int i, int *m0, int *n0) {
-    const int t = blockIdx.x + i * gridDim.x;
-    const int per_group = p.group_m * p.tiles_n;
-    const int group = t / per_group;
-    const int first = group * p.group_m;
-    const int rows = min(p.tiles_m - first, p.group_m);
-    const int in = t - group * per_group;
-    *m0 = (first + in % rows) * kBM;
-    *n0 = (in / rows) * kBN;
+  auto tileOrigin = [&](int tile, int *m0, int *n0) {
+    int tm, tn;
+    rasterTile(p, tile, &tm, &tn);
+    *m0 = tm * kBM;
+    *n0 = tn * kBN;
   };
   bool ok = true;
   auto wait = [&](uint64_t *bar, int parity) {
@@ -162,10 +165,11 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       int g = 0;  // k slices issued so far
-      for (int i = 0; i < my_tiles; ++i) {
+      for (int i = 0; i < nitems; ++i) {
+        const Item it = itemAt(p, cta, i);
         int m0, n0;
-        tileOrigin(i, &m0, &n0);
-        for (int kb = 0; kb < p.kiters; ++kb, ++g) {
+        tileOrigin(it.tile, &m0, &n0);
+        for (int kb = it.kb; kb < it.ke; ++kb, ++g) {
           const int s = g % kStages;
           if (g >= kStages) wait(&empty[s], (g / kStages - 1) & 1);
           unsigned char *sa = smem + s * kStageBytes;
@@ -192,12 +196,13 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
     if (lane == 0) {
       constexpr uint32_t idesc = instrDesc<kBN, kAMN, kBMN>();
       int g = 0;
-      for (int i = 0; i < my_tiles; ++i) {
+      for (int i = 0; i < nitems; ++i) {
+        const Item it = itemAt(p, cta, i);
         const int b = i % kAccums;
         if (i >= kAccums) wait(&acc_empty[b], (i / kAccums - 1) & 1);
         tcgenFenceAfter();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kBN);
-        for (int kb = 0; kb < p.kiters; ++kb, ++g) {
+        for (int kb = it.kb; kb < it.ke; ++kb, ++g) {
           const int s = g % kStages;
           wait(&full[s], (g / kStages) & 1);
           tcgenFenceAfter();
@@ -211,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
             const uint32_t koff_b = kBMN ? kk * 1024u : kk * 32u;
             const uint64_t ad = smemDesc<kAMN>(sa + koff);
             const uint64_t bd = smemDesc<kBMN>(sb + koff_b);
-            mmaTf32(d_tmem, ad, bd, idesc, kb > 0 || kk > 0);
+            mmaTf32(d_tmem, ad, bd, idesc, kb > it.kb || kk > 0);
           }
           mmaCommit(&empty[s]);  // the stage is free once these MMAs completed
         }
@@ -221,39 +226,128 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
   } else if (warp >= kEpilogueWarp0) {
     // ---------------- epilogue ----------------
     const int quarter = warp % 4;   // TMEM lanes [32*quarter, 32*quarter + 32)
-    const float alpha = p.alpha, beta = p.beta;
-    for (int i = 0; i < my_tiles; ++i) {
+    const int r = quarter * 32 + lane;   // this thread's row of the tile
+    const int etid = threadIdx.x - 32 * kEpilogueWarp0;   // 0..127
+    constexpr size_t kSlotFloats = static_cast<size_t>(kBM) * kBN;
+    // C = alpha * acc + beta * C for 32 columns of this thread's row.
+    auto storeChunk = [&](int row, int col0, const float (&acc)[32]) {
+      const bool row_ok = row < p.m;
+      float *cp = p.c + static_cast<size_t>(col0) * p.ldc + row;
+      float cv[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        cv[j] = 0.0F;
+        if constexpr (kBeta != Beta::kZero)
+          if (row_ok && col0 + j < p.n) cv[j] = cp[static_cast<size_t>(j) * p.ldc];
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (row_ok && col0 + j < p.n)
+          cp[static_cast<size_t>(j) * p.ldc] = epilogueValue<kBeta>(acc[j], p.alpha, p.beta, cv[j]);
+      }
+    };
+    for (int i = 0; i < nitems; ++i) {
+      const Item it = itemAt(p, cta, i);
       const int b = i % kAccums;
       int m0, n0;
-      tileOrigin(i, &m0, &n0);
+      tileOrigin(it.tile, &m0, &n0);
       wait(&acc_full[b], (i / kAccums) & 1);
       tcgenFenceAfter();
-      const int row = m0 + quarter * 32 + lane;
-      const bool row_ok = row < p.m;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(b * kBN);
+      if (it.kb == 0 && it.ke == p.kiters) {
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t v[32];
+          tmemLoad32(taddr + c * 32, v);
+          float acc[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(v[j]);
+          storeChunk(m0 + r, n0 + c * 32, acc);
+        }
+        tcgenFenceBefore();
+        mbarArrive(&acc_empty[b]);
+        continue;
+      }
+      // Stream-K piece: publish it, free the accumulator, count the arrival;
+      // the last arriving piece sums every piece in piece order and writes C.
+      // Slot layout: float4 q of chunk c of thread r at [(c*8 + q)*128 + r],
+      // so each warp access is 512 contiguous bytes.
+      const int u = it.tile - p.dp_tiles;
+      float4 *slot = reinterpret_cast<float4 *>(p.ws) +
+                     static_cast<size_t>(skSlot(p, cta, u)) * (kSlotFloats / 4);
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         uint32_t v[32];
-        tmemLoad32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                       static_cast<uint32_t>(b * kBN + c * 32),
-                   v);
-        const int col0 = n0 + c * 32;
-        float *cp = p.c + static_cast<size_t>(col0) * p.ldc + row;
-        float cv[32];
+        tmemLoad32(taddr + c * 32, v);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          cv[j] = 0.0F;
-          if constexpr (kBeta != Beta::kZero)
-            if (row_ok && col0 + j < p.n) cv[j] = cp[static_cast<size_t>(j) * p.ldc];
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (row_ok && col0 + j < p.n)
-            cp[static_cast<size_t>(j) * p.ldc] =
-                epilogueValue<kBeta>(__uint_as_float(v[j]), alpha, beta, cv[j]);
-        }
+        for (int q = 0; q < 8; ++q)
+          __stcg(slot + (c * 8 + q) * kBM + r,
+                 make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                             __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])));
       }
       tcgenFenceBefore();
       mbarArrive(&acc_empty[b]);
+      const int first = skOwner(p, u * p.kiters);
+      const int last = skOwner(p, (u + 1) * p.kiters - 1);
+      __threadfence();
+      namedBarrier<1, 128>();
+      if (etid == 0) last_arrival = atomicAdd(p.counters + u, 1) == last - first;
+      namedBarrier<1, 128>();
+      if (last_arrival) {
+        __threadfence();
+        auto piece = [&](int pc) {
+          return reinterpret_cast<const float4 *>(p.ws) +
+                 static_cast<size_t>(skSlot(p, pc, u)) * (kSlotFloats / 4);
+        };
+        // Two chunks per pass, two pieces per round trip to L2 (the sum
+        // order per element stays piece order).
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; c += 2) {
+          float4 acc[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) acc[e] = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+#pragma unroll 1
+          for (int pc = first; pc <= last; pc += 2) {
+            const bool two = pc + 1 <= last;
+            const float4 *s0 = piece(pc) + c * 8 * kBM + r;
+            const float4 *s1 = piece(two ? pc + 1 : pc) + c * 8 * kBM + r;
+            float4 v0[16], v1[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              v0[e] = __ldcg(s0 + e * kBM);
+              v1[e] = two ? __ldcg(s1 + e * kBM) : make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+            }
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              acc[e].x += v0[e].x;
+              acc[e].y += v0[e].y;
+              acc[e].z += v0[e].z;
+              acc[e].w += v0[e].w;
+              if (two) {
+                acc[e].x += v1[e].x;
+                acc[e].y += v1[e].y;
+                acc[e].z += v1[e].z;
+                acc[e].w += v1[e].w;
+              }
+            }
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float out[32];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              out[4 * q] = acc[h * 8 + q].x;
+              out[4 * q + 1] = acc[h * 8 + q].y;
+              out[4 * q + 2] = acc[h * 8 + q].z;
+              out[4 * q + 3] = acc[h * 8 + q].w;
+            }
+            storeChunk(m0 + r, n0 + (c + h) * 32, out);
+          }
+        }
+        if (etid == 0) p.counters[u] = 0;  // ready for the next launch
+      }
+      namedBarrier<1, 128>();   // last_arrival is reused by the next piece
     }
   }
 

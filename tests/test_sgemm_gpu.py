@@ -343,3 +343,39 @@ def test_reference_benchmark_runs_against_product(cuda):
     assert meta["device"]["compute_capability_major"] == 10
     assert (res["m"], res["n"], res["k"]) == (512, 384, 256)
     assert res["sgblas_gflops"] > 0 and res["cublas_gflops"] > 0 and res["ratio"] > 0
+
+
+# ---- 64-bit addressing and grid limits ---------------------------------------
+@pytest.mark.parametrize("math", ["fp32", "tf32"])
+def test_huge_outputs(cuda, handle, math):
+    """C with more than 2^31 elements (64-bit offsets in the epilogue), and n
+    of five million columns (far past the 65535 grid-Y limit a 2-D launch of
+    the reference has to work around); sampled against the oracle, including
+    the last row and column."""
+    torch = cuda
+    handle.set_math_mode(sg.SGBLAS_MATH_TF32 if math == "tf32" else sg.SGBLAS_MATH_FP32)
+    try:
+        for (m, n, k) in ((50000, 44000, 4), (8, 5_000_000, 8)):
+            rng = np.random.default_rng(m + n)
+            a = rng.uniform(-1, 1, m * k).astype(np.float32)
+            b = rng.uniform(-1, 1, k * n).astype(np.float32)
+            da = torch.from_numpy(a).cuda()
+            db = torch.from_numpy(b).cuda()
+            dc = torch.full((m * n,), float("nan"), dtype=torch.float32, device="cuda")
+            handle.sgemm(0, 0, m, n, k, 1.0, da, m, db, k, 0.0, dc, m)
+            torch.cuda.synchronize()
+            rows = np.concatenate([rng.integers(0, m, 4000), [0, m - 1, m - 1, 0]])
+            cols = np.concatenate([rng.integers(0, n, 4000), [0, n - 1, 0, n - 1]])
+            flat = torch.from_numpy(rows.astype(np.int64) + cols.astype(np.int64) * m).cuda()
+            got = dc[flat].cpu().numpy().astype(np.float64)
+            c0 = np.zeros(1, np.float32)
+            ref, mag = oracle.sgemm_f64_points(0, 0, k, 1.0, a, m, b, k, 0.0, c0, m, rows, cols)
+            tol = (2.0 ** -9 + (k + 2) * 2.0 ** -22) * mag if math == "tf32" else \
+                oracle.tol_north_star(k, mag)
+            assert np.all(np.abs(got - ref) <= tol), (m, n, k, math)
+            assert not torch.isnan(dc).any().item(), (m, n, k, math)
+            del dc
+            torch.cuda.empty_cache()
+    finally:
+        handle.set_math_mode(sg.SGBLAS_MATH_FP32)
+    assert sg.get_device_errors() == 0
