@@ -14,6 +14,7 @@ be bit-identical; beta == 0 must overwrite NaN-poisoned C.
 import numpy as np
 import pytest
 
+import oracle
 import sgblas_b200 as sg
 from tests import cases as C
 from tests.gpu_util import check_full, check_sampled, run_sgemm, to_device
