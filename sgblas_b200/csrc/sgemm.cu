@@ -185,10 +185,28 @@ int smCount(int device) {
   return v;
 }
 
+namespace {
+
+// True while `stream` is being captured into a CUDA graph (or when that
+// cannot be told, to be safe). During a capture the workspace is neither
+// allocated nor ordered by its event: the graph's own edges order it, and an
+// allocation made inside a capture would belong to the graph.
+bool capturing(cudaStream_t stream) {
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &status) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return true;
+  }
+  return status != cudaStreamCaptureStatusNone;
+}
+
+}  // namespace
+
 bool ensureWorkspace(sgblasContext *ctx, size_t need, int device, cudaStream_t stream) {
+  const bool in_capture = capturing(stream);
   if (ctx->workspace != nullptr && ctx->workspace_device == device &&
       ctx->workspace_bytes >= need) {
-    if (ctx->workspace_event != nullptr &&
+    if (!in_capture && ctx->workspace_event != nullptr &&
         cudaStreamWaitEvent(stream, static_cast<cudaEvent_t>(ctx->workspace_event), 0) !=
             cudaSuccess) {
       (void)cudaGetLastError();
@@ -196,6 +214,7 @@ bool ensureWorkspace(sgblasContext *ctx, size_t need, int device, cudaStream_t s
     }
     return true;
   }
+  if (in_capture) return false;   // the caller falls back to a path without it
   if (ctx->workspace != nullptr && ctx->workspace_device == device) {
     // Growing: free the old buffer stream-ordered after its last user, so the
     // call does not block the host.
@@ -242,6 +261,7 @@ bool ensureWorkspace(sgblasContext *ctx, size_t need, int device, cudaStream_t s
 }
 
 bool markWorkspaceUse(sgblasContext *ctx, cudaStream_t stream) {
+  if (capturing(stream)) return true;
   if (cudaEventRecord(static_cast<cudaEvent_t>(ctx->workspace_event), stream) != cudaSuccess) {
     (void)cudaGetLastError();
     return false;

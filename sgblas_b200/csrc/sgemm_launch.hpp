@@ -91,7 +91,9 @@ sgblasStatus_t launchPack(const float *src, int ld, bool k_contiguous, int rows_
 
 // Provides [counters | 2*grid slots] for a stream-K launch on `stream`.
 // The handle workspace is grow-only and allocated stream-ordered; false when
-// it cannot be provided (the caller then schedules whole tiles only).
+// it cannot be provided (the caller then schedules whole tiles only). While
+// `stream` is being captured into a CUDA graph it is never allocated or
+// grown, and launches are not ordered by its event (the graph orders them).
 bool ensureWorkspace(sgblasContext *ctx, size_t bytes, int device, cudaStream_t stream);
 // Marks the end of a launch that used the handle workspace.
 bool markWorkspaceUse(sgblasContext *ctx, cudaStream_t stream);

@@ -380,3 +380,42 @@ def test_huge_outputs(cuda, handle, math):
     finally:
         handle.set_math_mode(sg.SGBLAS_MATH_FP32)
     assert sg.get_device_errors() == 0
+
+
+def test_cuda_graph_capture_and_replay(cuda, handle):
+    """After a first call has set up the workspace, products (FP32 with a
+    stream-K split and an operand copy, and TF32) can be captured in a CUDA
+    graph and replayed with new inputs."""
+    torch = cuda
+    stream = torch.cuda.Stream()
+    handle.set_stream(stream)
+    try:
+        for math, (m, n, k, ldb_pad) in (("fp32", (1000, 700, 900, 1)), ("tf32", (512, 512, 512, 0))):
+            handle.set_math_mode(sg.SGBLAS_MATH_TF32 if math == "tf32" else sg.SGBLAS_MATH_FP32)
+            case = C.Case("graph", 0, 0, m, n, k, m, k + ldb_pad, m, 1.0, 0.0)
+            a, b, c = C.cfg_inputs(case, 55, -1)
+            da, pa = to_device(torch, a)
+            db, pb = to_device(torch, b)
+            dc, pc = to_device(torch, c)
+            with torch.cuda.stream(stream):
+                handle.sgemm(0, 0, m, n, k, 1.0, pa, case.lda, pb, case.ldb, 0.0, pc, m)  # set-up
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                handle.sgemm(0, 0, m, n, k, 1.0, pa, case.lda, pb, case.ldb, 0.0, pc, m)
+            a2, b2, _ = C.cfg_inputs(case, 56, -1)
+            da.copy_(torch.from_numpy(a2))
+            db.copy_(torch.from_numpy(b2))
+            dc.fill_(float("nan"))
+            graph.replay()
+            torch.cuda.synchronize()
+            ref, mag = oracle.sgemm_f64(0, 0, m, n, k, 1.0, a2, case.lda, b2, case.ldb, 0.0, c, m)
+            got = dc.cpu().numpy().reshape(n, m).T.astype(np.float64)
+            bound = (2.0 ** -9 + (k + 2) * 2.0 ** -22) * mag if math == "tf32" else \
+                oracle.tol_north_star(k, mag)
+            assert np.all(np.abs(got - ref) <= bound), math
+            del graph
+    finally:
+        handle.set_math_mode(sg.SGBLAS_MATH_FP32)
+        handle.set_stream(None)
+    assert sg.get_device_errors() == 0
