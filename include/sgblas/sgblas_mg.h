@@ -49,6 +49,11 @@ sgblasStatus_t sgblasMgSetStream(sgblasMgHandle_t handle, sgblasStream_t stream)
 
 sgblasStatus_t sgblasMgGetRank(sgblasMgHandle_t handle, int *rank, int *nranks);
 
+/* Math mode of the local products (SGBLAS_MATH_FP32, the default, or
+ * SGBLAS_MATH_TF32 for the tensor-core lane); same values and statuses as
+ * sgblasSetMathMode. Set it to the same value on every rank. */
+sgblasStatus_t sgblasMgSetMathMode(sgblasMgHandle_t handle, sgblasMath_t mode);
+
 /*
  * Collective, column-sharded SGEMM. On every rank `a` points to lda * (transa
  * == N ? k : m) floats of device memory: on `root` it holds A, on the others

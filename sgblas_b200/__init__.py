@@ -79,6 +79,7 @@ _SIGNATURES = {
                                        ctypes.c_void_p, ctypes.c_int]),
     "sgblasMgDestroy": (ctypes.c_int, [ctypes.c_void_p]),
     "sgblasMgSetStream": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "sgblasMgSetMathMode": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "sgblasMgGetRank": (ctypes.c_int, [ctypes.c_void_p, _c_int_p, _c_int_p]),
     "sgblasMgSgemm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_int, ctypes.c_int, _c_float_p, ctypes.c_void_p,
@@ -237,6 +238,9 @@ class MgHandle:
         if self._h is not None and self._h.value is not None:
             _check("sgblasMgDestroy", lib.sgblasMgDestroy(self._h))
         self._h = None
+
+    def set_math_mode(self, mode: int) -> None:
+        _check("sgblasMgSetMathMode", lib.sgblasMgSetMathMode(self._h, mode))
 
     def set_stream(self, stream) -> None:
         _check("sgblasMgSetStream",

@@ -129,6 +129,11 @@ extern "C" sgblasStatus_t sgblasMgSetStream(sgblasMgHandle_t handle, sgblasStrea
   return sgblasSetStream(handle->inner, stream);
 }
 
+extern "C" sgblasStatus_t sgblasMgSetMathMode(sgblasMgHandle_t handle, sgblasMath_t mode) {
+  if (handle == nullptr) return SGBLAS_STATUS_NOT_INITIALIZED;
+  return sgblasSetMathMode(handle->inner, mode);
+}
+
 extern "C" sgblasStatus_t sgblasMgGetRank(sgblasMgHandle_t handle, int *rank, int *nranks) {
   if (handle == nullptr) return SGBLAS_STATUS_NOT_INITIALIZED;
   if (rank == nullptr || nranks == nullptr) return SGBLAS_STATUS_INVALID_VALUE;
