@@ -52,7 +52,7 @@ sgblasStatus_t sgblasMgGetRank(sgblasMgHandle_t handle, int *rank, int *nranks);
 /* Math mode of the local products (SGBLAS_MATH_FP32, the default, or
  * SGBLAS_MATH_TF32 for the tensor-core lane); same values and statuses as
  * sgblasSetMathMode. Set it to the same value on every rank. */
-sgblasStatus_t sgblasMgSetMathMode(sgblasMgHandle_t handle, sgblasMath_t mode);
+sgblasStatus_t sgblasMgSetMathMode(sgblasMgHandle_t handle, sgblasMathMode_t mode);
 
 /*
  * Collective, column-sharded SGEMM. On every rank `a` points to lda * (transa

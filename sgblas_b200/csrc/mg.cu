@@ -129,7 +129,7 @@ extern "C" sgblasStatus_t sgblasMgSetStream(sgblasMgHandle_t handle, sgblasStrea
   return sgblasSetStream(handle->inner, stream);
 }
 
-extern "C" sgblasStatus_t sgblasMgSetMathMode(sgblasMgHandle_t handle, sgblasMath_t mode) {
+extern "C" sgblasStatus_t sgblasMgSetMathMode(sgblasMgHandle_t handle, sgblasMathMode_t mode) {
   if (handle == nullptr) return SGBLAS_STATUS_NOT_INITIALIZED;
   return sgblasSetMathMode(handle->inner, mode);
 }
