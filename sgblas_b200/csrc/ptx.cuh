@@ -205,6 +205,64 @@ __device__ __forceinline__ void tmemLoad32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---- CTA pairs (clusters of two) and cta_group::2 ---------------------------
+// Shared-memory address of the same location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t clusterAddr(uint32_t local_smem, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem), "r"(rank));
+  return r;
+}
+// Whole-cluster barrier (every thread of both CTAs), release / acquire.
+__device__ __forceinline__ void clusterSync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier in any CTA of the cluster (cluster address).
+__device__ __forceinline__ void mbarArriveCluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+// TMA 2-D load into this CTA's shared memory whose completion is counted on
+// an mbarrier of either CTA of the pair (cluster address).
+__device__ __forceinline__ void tmaLoad2dPair(void *dst, const CUtensorMap *map,
+                                              uint32_t cluster_bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smemAddr(dst)),
+      "l"(map), "r"(cluster_bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tmemAllocPair(uint32_t *dst_smem, uint32_t columns) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smemAddr(dst_smem)),
+               "r"(columns)
+               : "memory");
+}
+__device__ __forceinline__ void tmemRelinquishPair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmemDeallocPair(uint32_t taddr, uint32_t columns) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(columns)
+               : "memory");
+}
+// The pair's MMA (M = 256 over both CTAs' TMEM), issued by the even CTA.
+__device__ __forceinline__ void mmaTf32Pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+// Arrives once on the mbarrier at `cluster_bar` (either CTA of the pair)
+// when every pair MMA this thread issued so far has completed.
+__device__ __forceinline__ void mmaCommitPair(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   cluster_bar)
+               : "memory");
+}
+
 // Asynchronous prefetch of [ptr, ptr + bytes) from global memory into L2.
 // ptr 16-byte aligned, bytes a non-zero multiple of 16; the range must lie
 // inside one allocation.

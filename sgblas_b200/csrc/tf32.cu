@@ -124,6 +124,59 @@ sgblasStatus_t launchByBeta(t::Tf32Params &q, const Scratch &scratch, int sms, i
   return launchTyped<kBN, kAMN, kBMN, Beta::kGeneral>(q, scratch, sms, device, stream);
 }
 
+// The pair-CTA kernel: clusters of two, whole 256 x 256 tiles over the pairs.
+template <bool kAMN, bool kBMN, kern::Beta kBeta>
+sgblasStatus_t launchPairTyped(t::Tf32Params &q, int sms, int device, cudaStream_t stream) {
+  auto kernel = t::tf32PairKernel<kAMN, kBMN, kBeta>;
+  static std::atomic<uint64_t> configured{0};
+  if (!configureKernel(reinterpret_cast<const void *>(kernel), device, t::Pair::kSmemBytes,
+                       &configured))
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  const long long tiles = static_cast<long long>(q.tiles_m) * q.tiles_n;
+  const int pairs = static_cast<int>(std::min<long long>(tiles, sms / 2));
+  q.grid = pairs;
+  q.dp_tiles = static_cast<int>(tiles);
+  q.sk_tiles = q.sk_q = q.sk_r = 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(t::kThreads);
+  cfg.dynamicSmemBytes = t::Pair::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2] = {};
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return launchStatus(cudaLaunchKernelEx(&cfg, kernel, q));
+}
+
+template <bool kAMN, bool kBMN>
+sgblasStatus_t launchPair(const kern::GemmParams &p, t::Tf32Params &q, int sms, int device,
+                          cudaStream_t stream) {
+  q.tiles_m = (p.m + 2 * t::kBM - 1) / (2 * t::kBM);
+  q.tiles_n = (p.n + t::Pair::kBN - 1) / t::Pair::kBN;
+  // Per CTA: A boxes of 128 rows (K-major) or 32 x 32 chunks (MN-major); B
+  // boxes of 128 columns (K-major) or 32 x 32 chunks (MN-major).
+  const auto sw_k = CU_TENSOR_MAP_SWIZZLE_128B;
+  const auto sw_mn = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+  const unsigned long long lda_b = static_cast<unsigned long long>(p.lda) * 4;
+  const unsigned long long ldb_b = static_cast<unsigned long long>(p.ldb) * 4;
+  const bool ok_a = kAMN ? encodeTiled2d(&q.tma_a, p.a, p.m, p.k, lda_b, 32, 32, sw_mn)
+                         : encodeTiled2d(&q.tma_a, p.a, p.k, p.m, lda_b, 32, t::kBM, sw_k);
+  const bool ok_b = kBMN ? encodeTiled2d(&q.tma_b, p.b, p.n, p.k, ldb_b, 32, 32, sw_mn)
+                         : encodeTiled2d(&q.tma_b, p.b, p.k, p.n, ldb_b, 32,
+                                         t::Pair::kBNHalf, sw_k);
+  if (!ok_a || !ok_b) return SGBLAS_STATUS_EXECUTION_FAILED;
+  using kern::Beta;
+  if (q.beta == 0.0F) return launchPairTyped<kAMN, kBMN, Beta::kZero>(q, sms, device, stream);
+  if (q.beta == 1.0F) return launchPairTyped<kAMN, kBMN, Beta::kOne>(q, sms, device, stream);
+  return launchPairTyped<kAMN, kBMN, Beta::kGeneral>(q, sms, device, stream);
+}
+
 template <int kBN>
 sgblasStatus_t launchSized(const kern::GemmParams &p, bool a_mn, bool b_mn, t::Tf32Params &q,
                            const Scratch &scratch, int sms, int device, cudaStream_t stream) {
@@ -176,6 +229,19 @@ sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, const Scr
   // A: op N keeps m contiguous (MN-major), op T keeps k contiguous (K-major);
   // B: op N keeps k contiguous (K-major), op T keeps n contiguous (MN-major).
   const bool a_mn = !ta, b_mn = tb;
+  // Pair-CTA 256 x 256 tiles (half the B traffic per FLOP) where whole tiles
+  // fill the pairs' waves: at least one full wave and a last wave at least
+  // 70 % full (its schedule has no stream-K split).
+  const int pairs = sms / 2;
+  const long long pair_tiles = static_cast<long long>((p.m + 255) / 256) * ((p.n + 255) / 256);
+  const long long pair_rem = pair_tiles % pairs;
+  if (pairs > 0 && pair_tiles >= pairs && pair_tiles <= INT_MAX &&
+      (pair_rem == 0 || 10 * pair_rem >= 7 * pairs)) {
+    if (a_mn && b_mn) return launchPair<true, true>(p, q, sms, device, stream);
+    if (a_mn) return launchPair<true, false>(p, q, sms, device, stream);
+    if (b_mn) return launchPair<false, true>(p, q, sms, device, stream);
+    return launchPair<false, false>(p, q, sms, device, stream);
+  }
   const long long wide_tiles = static_cast<long long>(q.tiles_m) * ((p.n + 255) / 256);
   if (wide_tiles < sms && waves(128) * 77 < waves(256) * 100)
     return launchSized<128>(p, a_mn, b_mn, q, scratch, sms, device, stream);

@@ -359,6 +359,219 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
   }
 }
 
+// ---- pair-CTA variant: cta_group::2, 256 x 256 tiles ---------------------------
+// Two CTAs of a cluster share each 256 x 256 tile: CTA r (r = 0, 1) loads rows
+// [128 r, 128 r + 128) of the A tile and columns [128 r, 128 r + 128) of the B
+// tile into its own shared memory; the even CTA issues tcgen05.mma
+// cta_group::2 (M = 256, N = 256, K = 8), which reads A and B from both CTAs
+// and accumulates rows [128 r, 128 r + 128) in CTA r's TMEM. Per CTA this
+// moves half the B operand per FLOP of the single-CTA kernel. Both CTAs' TMA
+// loads complete on the even CTA's full[s]; the even CTA's MMA thread commits
+// each stage to both CTAs' empty[s] and each tile to both CTAs' acc_full[b];
+// both CTAs' epilogue threads arrive on the even CTA's acc_empty[b]. Whole
+// tiles only (no stream-K): the host uses it where the pairs' waves are full.
+struct Pair {
+  static constexpr int kBN = 256;             // tile width (UMMA N)
+  static constexpr int kBNHalf = 128;         // B columns per CTA
+  static constexpr int kBBytes = kBNHalf * kBK * 4;
+  static constexpr int kStageBytes = kABytes + kBBytes;   // 32 KiB
+  static constexpr int kStages = 6;
+  static constexpr int kTmemColumns = kAccums * kBN;      // 512
+  static constexpr int kBarrierBytes = 8 * (2 * kStages + 2 * kAccums);
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+};
+
+// M = 256 (two CTAs), N = 256.
+template <bool kAMN, bool kBMN>
+__host__ __device__ constexpr uint32_t instrDescPair() {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kAMN) << 15) |
+         (static_cast<uint32_t>(kBMN) << 16) | (static_cast<uint32_t>(Pair::kBN >> 3) << 17) |
+         (static_cast<uint32_t>(256 >> 4) << 24);
+}
+
+template <bool kAMN, bool kBMN, Beta kBeta>
+__global__ void __launch_bounds__(kThreads, 1)
+    tf32PairKernel(const __grid_constant__ Tf32Params p) {
+  constexpr int kStages = Pair::kStages;
+  constexpr int kStageBytes = Pair::kStageBytes;
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ uint32_t tmem_base_slot;
+  unsigned char *smem = smem_raw + ((1024 - (smemAddr(smem_raw) & 1023)) & 1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+  uint64_t *empty = full + kStages;
+  uint64_t *acc_full = empty + kStages;
+  uint64_t *acc_empty = acc_full + kAccums;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = blockIdx.x & 1;      // position in the CTA pair (cluster of 2)
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int nitems = numItems(p, pair);      // the schedule is over pairs
+  // Both CTAs of a pair have the same items, so both leave here or neither.
+  if (nitems == 0) return;
+
+  if (threadIdx.x == 0) {
+    prefetchTensorMap(&p.tma_a);
+    prefetchTensorMap(&p.tma_b);
+    for (int s = 0; s < kStages; ++s) {
+      mbarInit(&full[s], 1);
+      mbarInit(&empty[s], 1);
+    }
+    for (int b = 0; b < kAccums; ++b) {
+      mbarInit(&acc_full[b], 1);
+      mbarInit(&acc_empty[b], 2 * 32 * (kThreads / 32 - kEpilogueWarp0));
+    }
+    fenceBarrierInit();
+  }
+  if (warp == 2) {
+    tmemAllocPair(&tmem_base_slot, Pair::kTmemColumns);
+    tmemRelinquishPair();
+  }
+  tcgenFenceBefore();
+  __syncthreads();
+  clusterSync();   // both CTAs' barriers and TMEM exist before either uses the other's
+  tcgenFenceAfter();
+  const uint32_t tmem_base = tmem_base_slot;
+  gridDependencyWait();
+  allowDependentLaunch();
+
+  auto tileOrigin = [&](int tile, int *m0, int *n0) {
+    int tm, tn;
+    rasterTile(p, tile, &tm, &tn);
+    *m0 = tm * (2 * kBM);
+    *n0 = tn * Pair::kBN;
+  };
+  bool ok = true;
+  auto wait = [&](uint64_t *bar, int parity) {
+    if (ok) ok = mbarWait(bar, static_cast<uint32_t>(parity), p.err);
+  };
+  int total = 0;   // k slices of this pair
+  for (int i = 0; i < nitems; ++i) {
+    const Item it = itemAt(p, pair, i);
+    total += it.ke - it.kb;
+  }
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int g = 0;
+      for (int i = 0; i < nitems; ++i) {
+        const Item it = itemAt(p, pair, i);
+        int m0, n0;
+        tileOrigin(it.tile, &m0, &n0);
+        const int am0 = m0 + static_cast<int>(rank) * kBM;
+        const int bn0 = n0 + static_cast<int>(rank) * Pair::kBNHalf;
+        for (int kb = it.kb; kb < it.ke; ++kb, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages) wait(&empty[s], (g / kStages - 1) & 1);
+          unsigned char *sa = smem + s * kStageBytes;
+          unsigned char *sb = sa + kABytes;
+          const int k0 = kb * kBK;
+          const uint32_t bar0 = clusterAddr(smemAddr(&full[s]), 0);   // the even CTA's
+          if (rank == 0) mbarArriveExpectTx(&full[s], 2 * kStageBytes);
+          if constexpr (kAMN) {
+            for (int j = 0; j < kBM / 32; ++j)
+              tmaLoad2dPair(sa + j * kChunkBytes, &p.tma_a, bar0, am0 + 32 * j, k0);
+          } else {
+            tmaLoad2dPair(sa, &p.tma_a, bar0, k0, am0);
+          }
+          if constexpr (kBMN) {
+            for (int j = 0; j < Pair::kBNHalf / 32; ++j)
+              tmaLoad2dPair(sb + j * kChunkBytes, &p.tma_b, bar0, bn0 + 32 * j, k0);
+          } else {
+            tmaLoad2dPair(sb, &p.tma_b, bar0, k0, bn0);
+          }
+        }
+      }
+      // Drain: every commit the even CTA sent to this CTA's empty[s] has
+      // landed before the pair tears down.
+      for (int s = 0; s < kStages && s < total; ++s) {
+        const int g_last = total - 1 - ((total - 1 - s) % kStages);
+        wait(&empty[g_last % kStages], (g_last / kStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (even CTA) ----------------
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = instrDescPair<kAMN, kBMN>();
+      int g = 0;
+      for (int i = 0; i < nitems; ++i) {
+        const Item it = itemAt(p, pair, i);
+        const int b = i % kAccums;
+        if (i >= kAccums) wait(&acc_empty[b], (i / kAccums - 1) & 1);
+        tcgenFenceAfter();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * Pair::kBN);
+        for (int kb = it.kb; kb < it.ke; ++kb, ++g) {
+          const int s = g % kStages;
+          wait(&full[s], (g / kStages) & 1);
+          tcgenFenceAfter();
+          const uint32_t sa = smemAddr(smem + s * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kMmaK; ++kk) {
+            const uint32_t koff = kAMN ? kk * 1024u : kk * 32u;
+            const uint32_t koff_b = kBMN ? kk * 1024u : kk * 32u;
+            mmaTf32Pair(d_tmem, smemDesc<kAMN>(sa + koff), smemDesc<kBMN>(sb + koff_b), idesc,
+                        kb > it.kb || kk > 0);
+          }
+          const uint32_t e = smemAddr(&empty[s]);
+          mmaCommitPair(clusterAddr(e, 0));
+          mmaCommitPair(clusterAddr(e, 1));
+        }
+        const uint32_t f = smemAddr(&acc_full[b]);
+        mmaCommitPair(clusterAddr(f, 0));
+        mmaCommitPair(clusterAddr(f, 1));
+      }
+    }
+  } else if (warp >= kEpilogueWarp0) {
+    // ---------------- epilogue (both CTAs: 128 rows each) ----------------
+    const int quarter = warp % 4;
+    const int r = quarter * 32 + lane;
+    for (int i = 0; i < nitems; ++i) {
+      const Item it = itemAt(p, pair, i);
+      const int b = i % kAccums;
+      int m0, n0;
+      tileOrigin(it.tile, &m0, &n0);
+      wait(&acc_full[b], (i / kAccums) & 1);
+      tcgenFenceAfter();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(b * Pair::kBN);
+      const int row = m0 + static_cast<int>(rank) * kBM + r;
+      const bool row_ok = row < p.m;
+#pragma unroll 1
+      for (int c = 0; c < Pair::kBN / 32; ++c) {
+        uint32_t v[32];
+        tmemLoad32(taddr + c * 32, v);
+        const int col0 = n0 + c * 32;
+        float *cp = p.c + static_cast<size_t>(col0) * p.ldc + row;
+        float cv[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          cv[j] = 0.0F;
+          if constexpr (kBeta != Beta::kZero)
+            if (row_ok && col0 + j < p.n) cv[j] = cp[static_cast<size_t>(j) * p.ldc];
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (row_ok && col0 + j < p.n)
+            cp[static_cast<size_t>(j) * p.ldc] =
+                epilogueValue<kBeta>(__uint_as_float(v[j]), p.alpha, p.beta, cv[j]);
+        }
+      }
+      tcgenFenceBefore();
+      mbarArriveCluster(clusterAddr(smemAddr(&acc_empty[b]), 0));
+    }
+  }
+
+  tcgenFenceBefore();
+  __syncthreads();
+  clusterSync();   // neither CTA frees TMEM or exits while the pair still works
+  if (warp == 2) {
+    tcgenFenceAfter();
+    tmemDeallocPair(tmem_base, Pair::kTmemColumns);
+  }
+}
+
 }  // namespace sgblas::kern::tf32
 
 #endif  // SGBLAS_B200_TF32_TILE_CUH_

@@ -167,3 +167,33 @@ def test_tf32_wide_tiles(cuda, tf32_handle, ta, tb):
     got = out[rows + cols * m].astype(np.float64)
     assert np.all(np.abs(got - ref) <= tol_tf32(k, mag))
     assert np.all(np.isfinite(out))
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_tf32_pair_cta_tiles(cuda, tf32_handle, ta, tb):
+    """9472 x 512: exactly one wave of 256 x 256 tiles over the 74 CTA pairs,
+    so the cta_group::2 kernel runs; integer inputs make the TF32 products
+    exact, so C must equal the FP64 reference exactly, then a random case is
+    sampled against the TF32 bound."""
+    torch = cuda
+    m, n, k = 9472, 512, 96
+    lda, ldb = (k if ta else m), (n if tb else k)
+    rng = np.random.default_rng(40 + 2 * ta + tb)
+    a = rng.integers(-3, 4, lda * (m if ta else k)).astype(np.float32)
+    b = rng.integers(-3, 4, ldb * (k if tb else n)).astype(np.float32)
+    case = C.Case("tf32-pair", ta, tb, m, n, k, lda, ldb, m, 1.0, 0.0)
+    c = np.full(m * n, np.nan, np.float32)
+    status, out = run_sgemm(torch, tf32_handle, case, a, b, c)
+    assert status == 0
+    ref, _ = oracle.sgemm_f64(ta, tb, m, n, k, 1.0, a, lda, b, ldb, 0.0, c, m)
+    assert np.array_equal(c_view(out, m, n, m).astype(np.float64), ref)
+    case = C.Case("tf32-pair-rand", ta, tb, m, n, k, lda, ldb, m + 4, -0.5, 1.5)
+    a, b, c = C.cfg_inputs(case, 41, None)
+    status, out = run_sgemm(torch, tf32_handle, case, a, b, c)
+    assert status == 0
+    rows = np.concatenate([rng.integers(0, m, 4096), np.arange(0, m, 256), np.arange(255, m, 256)])
+    cols = np.concatenate([rng.integers(0, n, 4096), rng.integers(0, n, 2 * (m // 256))])
+    ref, mag = oracle.sgemm_f64_points(ta, tb, k, -0.5, a, lda, b, ldb, 1.5, c, m + 4, rows, cols)
+    got = out[rows + cols * (m + 4)].astype(np.float64)
+    assert np.all(np.abs(got - ref) <= tol_tf32(k, mag))
+    assert sg.get_device_errors() == 0
