@@ -17,6 +17,58 @@ namespace {
 
 namespace t = kern::tf32;
 
+Schedule makeScheduleTf32(long long tiles, int kiters, int sms);
+
+// Persistent schedule of `units` workers (CTAs, or CTA pairs) with the FP32
+// kernel's item structure and workspace layout ([counters | slots]), filled
+// into q; the workspace holds `slots` piece slots and `counters_per_tile`
+// counters per split tile. A tensor-core tile computes about ten times
+// faster than a CUDA-core one, so the piece fix-up costs relatively more:
+// only a partial last wave that leaves more than 30 % of the workers idle is
+// split (over all workers, each taking less than one tile), and a small
+// problem only when it would leave more than half of them idle. Without
+// scratch, whole tiles only. grid == 0 on failure.
+Schedule scheduleTf32(t::Tf32Params &q, long long tiles, int slots, int units,
+                      const Scratch &scratch, int device, cudaStream_t stream,
+                      bool *used_handle_workspace, int counters_per_tile = 1) {
+  Schedule s = makeScheduleTf32(tiles, q.kiters, units);
+  *used_handle_workspace = false;
+  if (s.sk_tiles > 0) {
+    const size_t need = kCounterRegionBytes + static_cast<size_t>(slots) * kSlotBytes;
+    const bool counters_fit = static_cast<size_t>(s.sk_tiles) * counters_per_tile * sizeof(int) <=
+                              kCounterRegionBytes;
+    unsigned char *base = nullptr;
+    if (scratch.fixed != nullptr) {
+      if (counters_fit && need <= scratch.fixed_bytes) {
+        if (cudaMemsetAsync(scratch.fixed, 0,
+                            static_cast<size_t>(s.sk_tiles) * counters_per_tile * sizeof(int),
+                            stream) != cudaSuccess) {
+          (void)cudaGetLastError();   // the memset's own error
+          return Schedule{};
+        }
+        base = scratch.fixed;
+      }
+    } else if (counters_fit && ensureWorkspace(scratch.ctx, need, device, stream)) {
+      base = static_cast<unsigned char *>(scratch.ctx->workspace);
+      *used_handle_workspace = true;
+    }
+    if (base != nullptr) {
+      q.counters = reinterpret_cast<int *>(base);
+      q.ws = reinterpret_cast<float *>(base + kCounterRegionBytes);
+    } else {
+      s = Schedule{};
+      s.grid = static_cast<int>(std::min<long long>(tiles, units));
+      s.dp_tiles = static_cast<int>(tiles);
+    }
+  }
+  q.grid = s.grid;
+  q.dp_tiles = s.dp_tiles;
+  q.sk_tiles = s.sk_tiles;
+  q.sk_q = s.sk_q;
+  q.sk_r = s.sk_r;
+  return s;
+}
+
 Schedule makeScheduleTf32(long long tiles, int kiters, int sms) {
   Schedule s;
   const int t = static_cast<int>(tiles);
@@ -51,51 +103,17 @@ template <int kBN, bool kAMN, bool kBMN, kern::Beta kBeta>
 sgblasStatus_t launchTyped(t::Tf32Params &q, const Scratch &scratch, int sms, int device,
                            cudaStream_t stream) {
   using G = t::Cfg<kBN>;
+  static_assert(static_cast<size_t>(t::kBM) * kBN * 4 <= kSlotBytes, "piece slot size");
   auto kernel = t::tf32Kernel<kBN, kAMN, kBMN, kBeta>;
   static std::atomic<uint64_t> configured{0};
   if (!configureKernel(reinterpret_cast<const void *>(kernel), device, G::kSmemBytes,
                        &configured))
     return SGBLAS_STATUS_EXECUTION_FAILED;
-  // Persistent schedule with the FP32 kernel's item structure and
-  // workspace layout ([counters | 2 * grid slots of 128 x kBN floats]), but a
-  // tensor-core tile computes about ten times faster than a CUDA-core one,
-  // so the piece fix-up costs relatively more: only a partial last wave that
-  // leaves more than 30 % of the SMs idle is split (over all CTAs, each
-  // taking less than one tile), and a small problem only when it would leave
-  // more than half of them idle.
   const long long tiles = static_cast<long long>(q.tiles_m) * q.tiles_n;
-  Schedule s = makeScheduleTf32(tiles, q.kiters, sms);
   bool used_handle_workspace = false;
-  if (s.sk_tiles > 0) {
-    static_assert(static_cast<size_t>(t::kBM) * kBN * 4 <= kSlotBytes, "piece slot size");
-    const size_t need = kCounterRegionBytes + 2 * static_cast<size_t>(s.grid) * kSlotBytes;
-    const bool counters_fit = static_cast<size_t>(s.sk_tiles) * sizeof(int) <= kCounterRegionBytes;
-    unsigned char *base = nullptr;
-    if (scratch.fixed != nullptr) {
-      if (counters_fit && need <= scratch.fixed_bytes) {
-        if (cudaMemsetAsync(scratch.fixed, 0, static_cast<size_t>(s.sk_tiles) * sizeof(int),
-                            stream) != cudaSuccess)
-          return launchStatus(cudaErrorUnknown);   // clears the memset's own error
-        base = scratch.fixed;
-      }
-    } else if (counters_fit && ensureWorkspace(scratch.ctx, need, device, stream)) {
-      base = static_cast<unsigned char *>(scratch.ctx->workspace);
-      used_handle_workspace = true;
-    }
-    if (base != nullptr) {
-      q.counters = reinterpret_cast<int *>(base);
-      q.ws = reinterpret_cast<float *>(base + kCounterRegionBytes);
-    } else {  // no scratch: whole tiles only
-      s = Schedule{};
-      s.grid = static_cast<int>(std::min<long long>(tiles, sms));
-      s.dp_tiles = static_cast<int>(tiles);
-    }
-  }
-  q.grid = s.grid;
-  q.dp_tiles = s.dp_tiles;
-  q.sk_tiles = s.sk_tiles;
-  q.sk_q = s.sk_q;
-  q.sk_r = s.sk_r;
+  const Schedule s = scheduleTf32(q, tiles, 2 * sms, sms, scratch, device, stream,
+                                  &used_handle_workspace);
+  if (s.grid == 0) return SGBLAS_STATUS_EXECUTION_FAILED;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(s.grid));
   cfg.blockDim = dim3(t::kThreads);
@@ -126,19 +144,23 @@ sgblasStatus_t launchByBeta(t::Tf32Params &q, const Scratch &scratch, int sms, i
 
 // The pair-CTA kernel: clusters of two, whole 256 x 256 tiles over the pairs.
 template <bool kAMN, bool kBMN, kern::Beta kBeta>
-sgblasStatus_t launchPairTyped(t::Tf32Params &q, int sms, int device, cudaStream_t stream) {
+sgblasStatus_t launchPairTyped(t::Tf32Params &q, const Scratch &scratch, int sms, int device,
+                               cudaStream_t stream) {
+  static_assert(static_cast<size_t>(t::kBM) * t::Pair::kBN * 4 <= kSlotBytes, "piece slot size");
   auto kernel = t::tf32PairKernel<kAMN, kBMN, kBeta>;
   static std::atomic<uint64_t> configured{0};
   if (!configureKernel(reinterpret_cast<const void *>(kernel), device, t::Pair::kSmemBytes,
                        &configured))
     return SGBLAS_STATUS_EXECUTION_FAILED;
   const long long tiles = static_cast<long long>(q.tiles_m) * q.tiles_n;
-  const int pairs = static_cast<int>(std::min<long long>(tiles, sms / 2));
-  q.grid = pairs;
-  q.dp_tiles = static_cast<int>(tiles);
-  q.sk_tiles = q.sk_q = q.sk_r = 0;
+  // Workers are CTA pairs; each CTA of a pair owns two slots and each split
+  // tile has a counter per half.
+  bool used_handle_workspace = false;
+  const Schedule s = scheduleTf32(q, tiles, 2 * 2 * (sms / 2), sms / 2, scratch, device, stream,
+                                  &used_handle_workspace, 2);
+  if (s.grid == 0) return SGBLAS_STATUS_EXECUTION_FAILED;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * s.grid));
   cfg.blockDim = dim3(t::kThreads);
   cfg.dynamicSmemBytes = t::Pair::kSmemBytes;
   cfg.stream = stream;
@@ -151,12 +173,16 @@ sgblasStatus_t launchPairTyped(t::Tf32Params &q, int sms, int device, cudaStream
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return launchStatus(cudaLaunchKernelEx(&cfg, kernel, q));
+  const sgblasStatus_t st = launchStatus(cudaLaunchKernelEx(&cfg, kernel, q));
+  if (st == SGBLAS_STATUS_SUCCESS && used_handle_workspace &&
+      !markWorkspaceUse(scratch.ctx, stream))
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  return st;
 }
 
 template <bool kAMN, bool kBMN>
-sgblasStatus_t launchPair(const kern::GemmParams &p, t::Tf32Params &q, int sms, int device,
-                          cudaStream_t stream) {
+sgblasStatus_t launchPair(const kern::GemmParams &p, t::Tf32Params &q, const Scratch &scratch,
+                          int sms, int device, cudaStream_t stream) {
   q.tiles_m = (p.m + 2 * t::kBM - 1) / (2 * t::kBM);
   q.tiles_n = (p.n + t::Pair::kBN - 1) / t::Pair::kBN;
   // Per CTA: A boxes of 128 rows (K-major) or 32 x 32 chunks (MN-major); B
@@ -172,9 +198,11 @@ sgblasStatus_t launchPair(const kern::GemmParams &p, t::Tf32Params &q, int sms, 
                                          t::Pair::kBNHalf, sw_k);
   if (!ok_a || !ok_b) return SGBLAS_STATUS_EXECUTION_FAILED;
   using kern::Beta;
-  if (q.beta == 0.0F) return launchPairTyped<kAMN, kBMN, Beta::kZero>(q, sms, device, stream);
-  if (q.beta == 1.0F) return launchPairTyped<kAMN, kBMN, Beta::kOne>(q, sms, device, stream);
-  return launchPairTyped<kAMN, kBMN, Beta::kGeneral>(q, sms, device, stream);
+  if (q.beta == 0.0F)
+    return launchPairTyped<kAMN, kBMN, Beta::kZero>(q, scratch, sms, device, stream);
+  if (q.beta == 1.0F)
+    return launchPairTyped<kAMN, kBMN, Beta::kOne>(q, scratch, sms, device, stream);
+  return launchPairTyped<kAMN, kBMN, Beta::kGeneral>(q, scratch, sms, device, stream);
 }
 
 template <int kBN>
@@ -229,18 +257,15 @@ sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, const Scr
   // A: op N keeps m contiguous (MN-major), op T keeps k contiguous (K-major);
   // B: op N keeps k contiguous (K-major), op T keeps n contiguous (MN-major).
   const bool a_mn = !ta, b_mn = tb;
-  // Pair-CTA 256 x 256 tiles (half the B traffic per FLOP) where whole tiles
-  // fill the pairs' waves: at least one full wave and a last wave at least
-  // 70 % full (its schedule has no stream-K split).
+  // Pair-CTA 256 x 256 tiles (half the B traffic per FLOP) once there is at
+  // least one tile per pair; the stream-K rule balances a partial last wave.
   const int pairs = sms / 2;
   const long long pair_tiles = static_cast<long long>((p.m + 255) / 256) * ((p.n + 255) / 256);
-  const long long pair_rem = pair_tiles % pairs;
-  if (pairs > 0 && pair_tiles >= pairs && pair_tiles <= INT_MAX &&
-      (pair_rem == 0 || 10 * pair_rem >= 7 * pairs)) {
-    if (a_mn && b_mn) return launchPair<true, true>(p, q, sms, device, stream);
-    if (a_mn) return launchPair<true, false>(p, q, sms, device, stream);
-    if (b_mn) return launchPair<false, true>(p, q, sms, device, stream);
-    return launchPair<false, false>(p, q, sms, device, stream);
+  if (pairs > 0 && pair_tiles >= pairs && pair_tiles <= INT_MAX) {
+    if (a_mn && b_mn) return launchPair<true, true>(p, q, scratch, sms, device, stream);
+    if (a_mn) return launchPair<true, false>(p, q, scratch, sms, device, stream);
+    if (b_mn) return launchPair<false, true>(p, q, scratch, sms, device, stream);
+    return launchPair<false, false>(p, q, scratch, sms, device, stream);
   }
   const long long wide_tiles = static_cast<long long>(q.tiles_m) * ((p.n + 255) / 256);
   if (wide_tiles < sms && waves(128) * 77 < waves(256) * 100)

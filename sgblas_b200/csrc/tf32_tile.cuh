@@ -368,8 +368,9 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
 // moves half the B operand per FLOP of the single-CTA kernel. Both CTAs' TMA
 // loads complete on the even CTA's full[s]; the even CTA's MMA thread commits
 // each stage to both CTAs' empty[s] and each tile to both CTAs' acc_full[b];
-// both CTAs' epilogue threads arrive on the even CTA's acc_empty[b]. Whole
-// tiles only (no stream-K): the host uses it where the pairs' waves are full.
+// both CTAs' epilogue threads arrive on the even CTA's acc_empty[b]. The
+// schedule is the single-CTA kernel's over pairs; each CTA publishes and sums
+// the stream-K pieces of its own half.
 struct Pair {
   static constexpr int kBN = 256;             // tile width (UMMA N)
   static constexpr int kBNHalf = 128;         // B columns per CTA
@@ -397,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kStageBytes = Pair::kStageBytes;
   extern __shared__ unsigned char smem_raw[];
   __shared__ uint32_t tmem_base_slot;
+  __shared__ int last_arrival;
   unsigned char *smem = smem_raw + ((1024 - (smemAddr(smem_raw) & 1023)) & 1023);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
   uint64_t *empty = full + kStages;
@@ -527,6 +529,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue (both CTAs: 128 rows each) ----------------
     const int quarter = warp % 4;
     const int r = quarter * 32 + lane;
+    const int etid = threadIdx.x - 32 * kEpilogueWarp0;   // 0..127
+    constexpr size_t kSlotFloat4 = static_cast<size_t>(kBM) * Pair::kBN / 4;
+    auto storeChunk = [&](int row, int col0, const float (&acc)[32]) {
+      const bool row_ok = row < p.m;
+      float *cp = p.c + static_cast<size_t>(col0) * p.ldc + row;
+      float cv[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        cv[j] = 0.0F;
+        if constexpr (kBeta != Beta::kZero)
+          if (row_ok && col0 + j < p.n) cv[j] = cp[static_cast<size_t>(j) * p.ldc];
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (row_ok && col0 + j < p.n)
+          cp[static_cast<size_t>(j) * p.ldc] = epilogueValue<kBeta>(acc[j], p.alpha, p.beta, cv[j]);
+      }
+    };
+    // This CTA's half of the slots: slot 2 * skSlot + rank.
+    auto slotOf = [&](int worker, int u) {
+      return reinterpret_cast<float4 *>(p.ws) +
+             static_cast<size_t>(2 * skSlot(p, worker, u) + static_cast<int>(rank)) * kSlotFloat4;
+    };
     for (int i = 0; i < nitems; ++i) {
       const Item it = itemAt(p, pair, i);
       const int b = i % kAccums;
@@ -537,29 +562,91 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(b * Pair::kBN);
       const int row = m0 + static_cast<int>(rank) * kBM + r;
-      const bool row_ok = row < p.m;
+      if (it.kb == 0 && it.ke == p.kiters) {
+#pragma unroll 1
+        for (int c = 0; c < Pair::kBN / 32; ++c) {
+          uint32_t v[32];
+          tmemLoad32(taddr + c * 32, v);
+          float acc[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(v[j]);
+          storeChunk(row, n0 + c * 32, acc);
+        }
+        tcgenFenceBefore();
+        mbarArriveCluster(clusterAddr(smemAddr(&acc_empty[b]), 0));
+        continue;
+      }
+      // Stream-K piece of this CTA's half: as in the single-CTA kernel, with
+      // a slot and an arrival counter per half.
+      const int u = it.tile - p.dp_tiles;
+      float4 *slot = slotOf(pair, u);
 #pragma unroll 1
       for (int c = 0; c < Pair::kBN / 32; ++c) {
         uint32_t v[32];
         tmemLoad32(taddr + c * 32, v);
-        const int col0 = n0 + c * 32;
-        float *cp = p.c + static_cast<size_t>(col0) * p.ldc + row;
-        float cv[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          cv[j] = 0.0F;
-          if constexpr (kBeta != Beta::kZero)
-            if (row_ok && col0 + j < p.n) cv[j] = cp[static_cast<size_t>(j) * p.ldc];
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (row_ok && col0 + j < p.n)
-            cp[static_cast<size_t>(j) * p.ldc] =
-                epilogueValue<kBeta>(__uint_as_float(v[j]), p.alpha, p.beta, cv[j]);
-        }
+        for (int q = 0; q < 8; ++q)
+          __stcg(slot + (c * 8 + q) * kBM + r,
+                 make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                             __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])));
       }
       tcgenFenceBefore();
       mbarArriveCluster(clusterAddr(smemAddr(&acc_empty[b]), 0));
+      const int first = skOwner(p, u * p.kiters);
+      const int last = skOwner(p, (u + 1) * p.kiters - 1);
+      int *counter = p.counters + 2 * u + static_cast<int>(rank);
+      __threadfence();
+      namedBarrier<1, 128>();
+      if (etid == 0) last_arrival = atomicAdd(counter, 1) == last - first;
+      namedBarrier<1, 128>();
+      if (last_arrival) {
+        __threadfence();
+#pragma unroll 1
+        for (int c = 0; c < Pair::kBN / 32; c += 2) {
+          float4 acc[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) acc[e] = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+#pragma unroll 1
+          for (int pc = first; pc <= last; pc += 2) {
+            const bool two = pc + 1 <= last;
+            const float4 *s0 = slotOf(pc, u) + c * 8 * kBM + r;
+            const float4 *s1 = slotOf(two ? pc + 1 : pc, u) + c * 8 * kBM + r;
+            float4 v0[16], v1[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              v0[e] = __ldcg(s0 + e * kBM);
+              v1[e] = two ? __ldcg(s1 + e * kBM) : make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+            }
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              acc[e].x += v0[e].x;
+              acc[e].y += v0[e].y;
+              acc[e].z += v0[e].z;
+              acc[e].w += v0[e].w;
+              if (two) {
+                acc[e].x += v1[e].x;
+                acc[e].y += v1[e].y;
+                acc[e].z += v1[e].z;
+                acc[e].w += v1[e].w;
+              }
+            }
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float out[32];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              out[4 * q] = acc[h * 8 + q].x;
+              out[4 * q + 1] = acc[h * 8 + q].y;
+              out[4 * q + 2] = acc[h * 8 + q].z;
+              out[4 * q + 3] = acc[h * 8 + q].w;
+            }
+            storeChunk(row, n0 + (c + h) * 32, out);
+          }
+        }
+        if (etid == 0) *counter = 0;  // ready for the next launch
+      }
+      namedBarrier<1, 128>();   // last_arrival is reused by the next piece
     }
   }
 

@@ -152,9 +152,9 @@ def test_tf32_no_alloc_and_batched(cuda, tf32_handle):
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 def test_tf32_wide_tiles(cuda, tf32_handle, ta, tb):
-    """4736 x 1024: exactly one wave of 256-wide tiles on 148 SMs, so the
-    256-wide kernel runs (small problems take the 128-wide one); sampled."""
-    m, n, k = 4736, 1024, 96
+    """2048 x 2048: 128 single-CTA 256-wide tiles for 148 SMs (fewer pair
+    tiles than pairs, too many tiles for the 128-wide kernel); sampled."""
+    m, n, k = 2048, 2048, 96
     lda, ldb = (k if ta else m), (n if tb else k)
     case = C.Case("tf32-wide", ta, tb, m, n, k, lda, ldb, m, 0.5, 2.0)
     a, b, c = C.cfg_inputs(case, 17, None)
@@ -196,4 +196,26 @@ def test_tf32_pair_cta_tiles(cuda, tf32_handle, ta, tb):
     ref, mag = oracle.sgemm_f64_points(ta, tb, k, -0.5, a, lda, b, ldb, 1.5, c, m + 4, rows, cols)
     got = out[rows + cols * (m + 4)].astype(np.float64)
     assert np.all(np.abs(got - ref) <= tol_tf32(k, mag))
+    assert sg.get_device_errors() == 0
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_tf32_pair_cta_stream_k(cuda, tf32_handle, ta, tb):
+    """4096 x 4096: 256 pair tiles are 3.46 waves of 74 pairs, so the last
+    wave is split by k over all pairs (each CTA publishes and sums its half);
+    integer inputs: exact."""
+    torch = cuda
+    m, n, k = 4096, 4096, 320
+    lda, ldb = (k if ta else m), (n if tb else k)
+    rng = np.random.default_rng(60 + 2 * ta + tb)
+    a = rng.integers(-2, 3, lda * (m if ta else k)).astype(np.float32)
+    b = rng.integers(-2, 3, ldb * (k if tb else n)).astype(np.float32)
+    c = rng.integers(-2, 3, m * n).astype(np.float32)
+    case = C.Case("tf32-pair-sk", ta, tb, m, n, k, lda, ldb, m, 1.0, 1.0)
+    status, out = run_sgemm(torch, tf32_handle, case, a, b, c)
+    assert status == 0
+    rows = np.concatenate([rng.integers(0, m, 8192), np.arange(0, m, 64)])
+    cols = np.concatenate([rng.integers(0, n, 8192), rng.integers(0, n, m // 64)])
+    ref, _ = oracle.sgemm_f64_points(ta, tb, k, 1.0, a, lda, b, ldb, 1.0, c, m, rows, cols)
+    assert np.array_equal(out[rows + cols * m].astype(np.float64), ref)
     assert sg.get_device_errors() == 0
