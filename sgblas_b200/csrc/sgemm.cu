@@ -58,6 +58,14 @@ namespace {
 
 sgblasStatus_t launchScale(int m, int n, float beta, float *c, int ldc, const Batch &batch,
                            cudaStream_t stream) {
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  }
+  const int arch = isSm100(device);
+  if (arch < 0) return SGBLAS_STATUS_EXECUTION_FAILED;
+  if (arch == 0) return SGBLAS_STATUS_ARCH_MISMATCH;
   const unsigned row_blocks = static_cast<unsigned>((m + 255) / 256);
   const dim3 grid(row_blocks < 1024u ? row_blocks : 1024u,
                   static_cast<unsigned>(n < 65535 ? n : 65535),
@@ -269,6 +277,25 @@ bool markWorkspaceUse(sgblasContext *ctx, cudaStream_t stream) {
   return true;
 }
 
+// The kernels are built for sm_100a only: 1 if `device` is compute
+// capability 10.0, 0 if not, -1 if it cannot be told. Cached per device.
+int isSm100(int device) {
+  static std::atomic<int> cached[kMaxDevices];   // 0 unknown, 1 yes, 2 no
+  if (device < 0 || device >= kMaxDevices) return -1;
+  int v = cached[device].load(std::memory_order_relaxed);
+  if (v == 0) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return -1;
+    }
+    v = (major == 10 && minor == 0) ? 1 : 2;
+    cached[device].store(v, std::memory_order_relaxed);
+  }
+  return v == 1 ? 1 : 0;
+}
+
 namespace {
 
 sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOperation_t tb,
@@ -280,6 +307,9 @@ sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOpe
     (void)cudaGetLastError();
     return SGBLAS_STATUS_EXECUTION_FAILED;
   }
+  const int arch = isSm100(device);
+  if (arch < 0) return SGBLAS_STATUS_EXECUTION_FAILED;
+  if (arch == 0) return SGBLAS_STATUS_ARCH_MISMATCH;
   unsigned *err = deviceErrorWord(device);
   if (err == nullptr) return SGBLAS_STATUS_EXECUTION_FAILED;
 

@@ -37,6 +37,10 @@ bool aligned16(const void *p);
 
 int smCount(int device);
 
+// 1 if `device` is compute capability 10.0 (what the kernels are built for),
+// 0 if not (callers return SGBLAS_STATUS_ARCH_MISMATCH), -1 on an error.
+int isSm100(int device);
+
 // Persistent schedule: one CTA per SM. Whole tiles are dealt round-robin;
 // when the tile count leaves a partial last wave, the last (full wave +
 // remainder) tiles are split by k iterations over all CTAs (stream-K), so every

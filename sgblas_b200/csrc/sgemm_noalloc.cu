@@ -90,6 +90,9 @@ extern "C" sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperat
     (void)cudaGetLastError();
     return SGBLAS_STATUS_EXECUTION_FAILED;
   }
+  const int arch = isSm100(device);
+  if (arch < 0) return SGBLAS_STATUS_EXECUTION_FAILED;
+  if (arch == 0) return SGBLAS_STATUS_ARCH_MISMATCH;
   unsigned *err = deviceErrorWord(device);
   if (err == nullptr) return SGBLAS_STATUS_EXECUTION_FAILED;
   unsigned char *scratch = scratchAddress(device);
