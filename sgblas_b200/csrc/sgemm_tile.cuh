@@ -28,16 +28,21 @@
 // a [k][x] buffer a few iterations ahead of its use.
 //
 // CTA: three warpgroups, one CTA per SM.
-//   - Warpgroups 0-1 (256 threads, 8 warps) compute a 256 (P) x 128 (D) tile;
-//     each thread owns a 16 (P) x 8 (D) block of C (64 FFMA2 per k step against
-//     4+2 shared loads). Warps form 2 (P) x 4 (D); lane bits lp = lane % 8,
-//     ld = lane / 8.
+//   - Warpgroups 0-1 (256 threads, 8 warps) compute a 256 (P) x 128 (D) tile
+//     (kTP = 16); each thread owns a 16 (P) x 8 (D) block of C (64 FFMA2 per
+//     k step against 4+2 shared loads). Warps form 2 (P) x 4 (D); lane bits
+//     lp = lane % 8, ld = lane / 8.
 //       P coordinates: 128*wp + 4*lp + {0..3} + 32*q, q = 0..3.
 //       D coordinates: 32*wd + 4*ld + {0..3} + {0, 16}.
+//     The kTP = 8 variant (small problems) computes 128 x 128 tiles with an
+//     8 x 8 block per thread.
 //   - Warpgroup 2 (128 threads) is the producer: one thread issues the TMA
 //     tile loads (or all 128 issue cp.async copies), and all 128 transpose
-//     [x][k] tiles into [k][x] buffers. It gives registers to the compute
+//     [x][k] tiles into [k][x] buffers. With beta != 0 it also prefetches
+//     each whole tile's block of C into L2. It gives registers to the compute
 //     warpgroups (setmaxnreg), so that those keep 232.
+//   Tiles of a strided or pointer-array batch are numbered batch-major in the
+//   same schedule; TMA tensor maps are 3-D (x, k, matrix).
 //   Producer and consumers meet only at mbarriers (stage full/empty,
 //   transposed buffer full/empty), so no warp ever waits on a CTA-wide
 //   barrier inside the main loop.
