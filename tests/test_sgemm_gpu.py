@@ -17,7 +17,7 @@ import pytest
 import oracle
 import sgblas_b200 as sg
 from tests import cases as C
-from tests.gpu_util import check_full, check_sampled, run_sgemm, to_device
+from tests.gpu_util import c_view, check_full, check_sampled, run_sgemm, to_device
 
 pytestmark = pytest.mark.gpu
 
@@ -418,4 +418,58 @@ def test_cuda_graph_capture_and_replay(cuda, handle):
     finally:
         handle.set_math_mode(sg.SGBLAS_MATH_FP32)
         handle.set_stream(None)
+    assert sg.get_device_errors() == 0
+
+
+def test_concurrent_handles_from_host_threads(cuda):
+    """Four host threads, each with its own handle and stream, issue products
+    concurrently (ctypes releases the GIL): stream-K splits, operand copies,
+    both math modes. The lazily initialised per-device state (kernel
+    attributes, tensor-map encoder, error word) must tolerate the race."""
+    import threading
+    torch = cuda
+    shapes = [(1000, 700, 900, 0, "fp32"), (333, 444, 123, 1, "fp32"), (512, 512, 512, 0, "tf32"),
+              (2048, 512, 256, 0, "fp32")]
+    results = {}
+
+    def worker(idx):
+        try:
+            m, n, k, pad, math = shapes[idx]
+            with sg.Handle() as h:
+                stream = torch.cuda.Stream()
+                h.set_stream(stream)
+                if math == "tf32":
+                    h.set_math_mode(sg.SGBLAS_MATH_TF32)
+                case = C.Case("threads", 0, 0, m, n, k, m + pad, k + pad, m, 1.0, 0.0)
+                a, b, c = C.cfg_inputs(case, 70 + idx, -1)
+                da, pa = to_device(torch, a)
+                db, pb = to_device(torch, b)
+                outs = []
+                for rep in range(10):
+                    dc, pc = to_device(torch, c)
+                    with torch.cuda.stream(stream):
+                        h.sgemm(0, 0, m, n, k, 1.0, pa, case.lda, pb, case.ldb, 0.0, pc, m)
+                    outs.append(dc)
+                stream.synchronize()
+                results[idx] = (case, a, b, c, [o.cpu().numpy() for o in outs], math)
+        except Exception as e:  # reported by the main thread
+            results[idx] = e
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in range(len(shapes))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=300)
+    for idx in range(len(shapes)):
+        res = results.get(idx)
+        assert not isinstance(res, Exception) and res is not None, (idx, res)
+        case, a, b, c, outs, math = res
+        ref, mag = oracle.sgemm_f64(0, 0, case.m, case.n, case.k, 1.0, a, case.lda, b, case.ldb,
+                                    0.0, c, case.ldc)
+        bound = (2.0 ** -9 + (case.k + 2) * 2.0 ** -22) * mag if math == "tf32" else \
+            oracle.tol_north_star(case.k, mag)
+        for out in outs:
+            assert np.array_equal(out, outs[0]), (idx, "repeat differs")
+            got = c_view(out, case.m, case.n, case.ldc).astype(np.float64)
+            assert np.all(np.abs(got - ref) <= bound), (idx, math)
     assert sg.get_device_errors() == 0
