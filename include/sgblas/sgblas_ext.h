@@ -58,7 +58,11 @@ sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperation_t trans
  * cublasSgemmStridedBatched / cublasSgemmBatched.
  *
  * Strided: matrix i is a + i*stride_a (b, c alike; strides in elements, any
- * sign; stride_a or stride_b 0 reuses one matrix for every product). */
+ * sign; stride_a or stride_b 0 reuses one matrix for every product). In
+ * SGBLAS_MATH_TF32 mode a strided batch runs on the tensor cores when its
+ * strides are positive multiples of 4 floats (and A, B are 16-byte aligned
+ * with leading dimensions that are multiples of 4); otherwise, and for
+ * pointer arrays, it computes in FP32. */
 sgblasStatus_t sgblasSgemmStridedBatched(sgblasHandle_t handle, sgblasOperation_t transa,
                                          sgblasOperation_t transb, int m, int n, int k,
                                          const float *alpha, const float *a, int lda,

@@ -232,6 +232,14 @@ __device__ __forceinline__ void tmaLoad2dPair(void *dst, const CUtensorMap *map,
       "l"(map), "r"(cluster_bar), "r"(x), "r"(y)
       : "memory");
 }
+__device__ __forceinline__ void tmaLoad3dPair(void *dst, const CUtensorMap *map,
+                                              uint32_t cluster_bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smemAddr(dst)),
+      "l"(map), "r"(cluster_bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 __device__ __forceinline__ void tmemAllocPair(uint32_t *dst_smem, uint32_t columns) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smemAddr(dst_smem)),

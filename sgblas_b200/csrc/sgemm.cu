@@ -135,16 +135,22 @@ bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool encodeTiled2d(CUtensorMap *map, const float *ptr, unsigned long long dim0,
-                   unsigned long long dim1, unsigned long long stride1_bytes, unsigned box0,
-                   unsigned box1, CUtensorMapSwizzle swizzle) {
+bool encodeTiled3d(CUtensorMap *map, const float *ptr, unsigned long long dim0,
+                   unsigned long long dim1, unsigned long long stride1_bytes, int batch,
+                   long long stride_elems, unsigned box0, unsigned box1,
+                   CUtensorMapSwizzle swizzle) {
   const EncodeTiledFn fn = encodeTiled();
   if (fn == nullptr) return false;
-  const cuuint64_t dims[2] = {dim0, dim1};
-  const cuuint64_t strides[1] = {stride1_bytes};
-  const cuuint32_t box[2] = {box0, box1};
-  const cuuint32_t elem_strides[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides, box,
+  // A single matrix is a batch of one with an unused, valid batch stride.
+  const long long stride2 = batch == 1
+                                ? static_cast<long long>((dim1 * stride1_bytes + 15) / 16 * 16)
+                                : stride_elems * 4;
+  if (stride2 <= 0 || stride2 % 16 != 0 || stride2 >= (1LL << 40)) return false;
+  const cuuint64_t dims[3] = {dim0, dim1, static_cast<cuuint64_t>(batch)};
+  const cuuint64_t strides[2] = {stride1_bytes, static_cast<cuuint64_t>(stride2)};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  const cuuint32_t elem_strides[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(ptr), dims, strides, box,
             elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -378,8 +384,15 @@ sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOpe
     }
   }
   sgblasStatus_t st;
-  if (ctx->math_mode == SGBLAS_MATH_TF32 && single &&
-      tf32Eligible(p.a, p.lda, p.b, p.ldb)) {
+  // TF32 for one matrix or a strided batch whose matrices TMA can all read
+  // (positive strides, multiples of 4 floats); otherwise FP32, which is
+  // more accurate than TF32 mode asks.
+  auto tf32Stride = [](long long stride) {
+    return stride > 0 && stride % 4 == 0 && stride < (1LL << 38);
+  };
+  if (ctx->math_mode == SGBLAS_MATH_TF32 && batch.a_ptrs == nullptr &&
+      tf32Eligible(p.a, p.lda, p.b, p.ldb) &&
+      (batch.count == 1 || (tf32Stride(batch.stride_a) && tf32Stride(batch.stride_b)))) {
     st = launchTf32(tA, tB, p, scratch, device, stream);
   } else if (!tA && !tB) st = launchMode<false, false>(p, scratch, device, stream);
   else if (!tA && tB) st = launchMode<false, true>(p, scratch, device, stream);

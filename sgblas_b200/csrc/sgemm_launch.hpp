@@ -26,10 +26,14 @@ sgblasStatus_t launchStatus(cudaError_t e);
 bool encodeMatrix(CUtensorMap *map, const float *ptr, int rows, int cols, int ld, int batch,
                   long long stride, int box_rows, int box_cols, bool swizzle64);
 
-// Plain 2-D tensor map (dim0 contiguous) with the given swizzle.
-bool encodeTiled2d(CUtensorMap *map, const float *ptr, unsigned long long dim0,
-                   unsigned long long dim1, unsigned long long stride1_bytes, unsigned box0,
-                   unsigned box1, CUtensorMapSwizzle swizzle);
+// 3-D tensor map of `batch` dim0 x dim1 FP32 matrices (dim0 contiguous, rows
+// stride1_bytes apart, matrix i at ptr + i * stride_elems floats) read in
+// box0 x box1 boxes of one matrix, with the given swizzle. False if the batch
+// stride or the driver refuses it.
+bool encodeTiled3d(CUtensorMap *map, const float *ptr, unsigned long long dim0,
+                   unsigned long long dim1, unsigned long long stride1_bytes, int batch,
+                   long long stride_elems, unsigned box0, unsigned box1,
+                   CUtensorMapSwizzle swizzle);
 
 bool aligned16(const void *p);
 
@@ -108,8 +112,9 @@ bool markWorkspaceUse(sgblasContext *ctx, cudaStream_t stream);
 inline bool tf32Eligible(const float *a, int lda, const float *b, int ldb) {
   return aligned16(a) && aligned16(b) && lda % 4 == 0 && ldb % 4 == 0;
 }
-// One product in TF32 (single matrix; p carries pointers, sizes, scalars and
-// the error word).
+// One product, or a strided batch, in TF32 (p carries pointers, sizes,
+// scalars, batch strides and the error word). Pointer-array batches are not
+// handled here.
 sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, const Scratch &scratch,
                           int device, cudaStream_t stream);
 

@@ -99,17 +99,17 @@ Schedule makeScheduleTf32(long long tiles, int kiters, int sms) {
   return s;
 }
 
-template <int kBN, bool kAMN, bool kBMN, kern::Beta kBeta>
+template <int kBN, bool kAMN, bool kBMN, kern::Beta kBeta, bool kBatch>
 sgblasStatus_t launchTyped(t::Tf32Params &q, const Scratch &scratch, int sms, int device,
                            cudaStream_t stream) {
   using G = t::Cfg<kBN>;
   static_assert(static_cast<size_t>(t::kBM) * kBN * 4 <= kSlotBytes, "piece slot size");
-  auto kernel = t::tf32Kernel<kBN, kAMN, kBMN, kBeta>;
+  auto kernel = t::tf32Kernel<kBN, kAMN, kBMN, kBeta, kBatch>;
   static std::atomic<uint64_t> configured{0};
   if (!configureKernel(reinterpret_cast<const void *>(kernel), device, G::kSmemBytes,
                        &configured))
     return SGBLAS_STATUS_EXECUTION_FAILED;
-  const long long tiles = static_cast<long long>(q.tiles_m) * q.tiles_n;
+  const long long tiles = static_cast<long long>(q.tiles_m) * q.tiles_n * q.batch;
   bool used_handle_workspace = false;
   const Schedule s = scheduleTf32(q, tiles, 2 * sms, sms, scratch, device, stream,
                                   &used_handle_workspace);
@@ -131,28 +131,35 @@ sgblasStatus_t launchTyped(t::Tf32Params &q, const Scratch &scratch, int sms, in
   return st;
 }
 
+template <int kBN, bool kAMN, bool kBMN, kern::Beta kBeta>
+sgblasStatus_t launchByBatch(t::Tf32Params &q, const Scratch &scratch, int sms, int device,
+                             cudaStream_t stream) {
+  if (q.batch > 1) return launchTyped<kBN, kAMN, kBMN, kBeta, true>(q, scratch, sms, device, stream);
+  return launchTyped<kBN, kAMN, kBMN, kBeta, false>(q, scratch, sms, device, stream);
+}
+
 template <int kBN, bool kAMN, bool kBMN>
 sgblasStatus_t launchByBeta(t::Tf32Params &q, const Scratch &scratch, int sms, int device,
                             cudaStream_t stream) {
   using kern::Beta;
   if (q.beta == 0.0F)
-    return launchTyped<kBN, kAMN, kBMN, Beta::kZero>(q, scratch, sms, device, stream);
+    return launchByBatch<kBN, kAMN, kBMN, Beta::kZero>(q, scratch, sms, device, stream);
   if (q.beta == 1.0F)
-    return launchTyped<kBN, kAMN, kBMN, Beta::kOne>(q, scratch, sms, device, stream);
-  return launchTyped<kBN, kAMN, kBMN, Beta::kGeneral>(q, scratch, sms, device, stream);
+    return launchByBatch<kBN, kAMN, kBMN, Beta::kOne>(q, scratch, sms, device, stream);
+  return launchByBatch<kBN, kAMN, kBMN, Beta::kGeneral>(q, scratch, sms, device, stream);
 }
 
 // The pair-CTA kernel: clusters of two, whole 256 x 256 tiles over the pairs.
-template <bool kAMN, bool kBMN, kern::Beta kBeta>
+template <bool kAMN, bool kBMN, kern::Beta kBeta, bool kBatch>
 sgblasStatus_t launchPairTyped(t::Tf32Params &q, const Scratch &scratch, int sms, int device,
                                cudaStream_t stream) {
   static_assert(static_cast<size_t>(t::kBM) * t::Pair::kBN * 4 <= kSlotBytes, "piece slot size");
-  auto kernel = t::tf32PairKernel<kAMN, kBMN, kBeta>;
+  auto kernel = t::tf32PairKernel<kAMN, kBMN, kBeta, kBatch>;
   static std::atomic<uint64_t> configured{0};
   if (!configureKernel(reinterpret_cast<const void *>(kernel), device, t::Pair::kSmemBytes,
                        &configured))
     return SGBLAS_STATUS_EXECUTION_FAILED;
-  const long long tiles = static_cast<long long>(q.tiles_m) * q.tiles_n;
+  const long long tiles = static_cast<long long>(q.tiles_m) * q.tiles_n * q.batch;
   // Workers are CTA pairs; each CTA of a pair owns two slots and each split
   // tile has a counter per half.
   bool used_handle_workspace = false;
@@ -191,18 +198,25 @@ sgblasStatus_t launchPair(const kern::GemmParams &p, t::Tf32Params &q, const Scr
   const auto sw_mn = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   const unsigned long long lda_b = static_cast<unsigned long long>(p.lda) * 4;
   const unsigned long long ldb_b = static_cast<unsigned long long>(p.ldb) * 4;
-  const bool ok_a = kAMN ? encodeTiled2d(&q.tma_a, p.a, p.m, p.k, lda_b, 32, 32, sw_mn)
-                         : encodeTiled2d(&q.tma_a, p.a, p.k, p.m, lda_b, 32, t::kBM, sw_k);
-  const bool ok_b = kBMN ? encodeTiled2d(&q.tma_b, p.b, p.n, p.k, ldb_b, 32, 32, sw_mn)
-                         : encodeTiled2d(&q.tma_b, p.b, p.k, p.n, ldb_b, 32,
-                                         t::Pair::kBNHalf, sw_k);
+  const bool ok_a = kAMN ? encodeTiled3d(&q.tma_a, p.a, p.m, p.k, lda_b, p.batch, p.stride_a, 32, 32, sw_mn)
+                         : encodeTiled3d(&q.tma_a, p.a, p.k, p.m, lda_b, p.batch, p.stride_a, 32, t::kBM, sw_k);
+  const bool ok_b = kBMN ? encodeTiled3d(&q.tma_b, p.b, p.n, p.k, ldb_b, p.batch, p.stride_b, 32, 32, sw_mn)
+                         : encodeTiled3d(&q.tma_b, p.b, p.k, p.n, ldb_b, p.batch,
+                                         p.stride_b, 32, t::Pair::kBNHalf, sw_k);
   if (!ok_a || !ok_b) return SGBLAS_STATUS_EXECUTION_FAILED;
   using kern::Beta;
+  const bool batched = q.batch > 1;
   if (q.beta == 0.0F)
-    return launchPairTyped<kAMN, kBMN, Beta::kZero>(q, scratch, sms, device, stream);
+    return batched ? launchPairTyped<kAMN, kBMN, Beta::kZero, true>(q, scratch, sms, device, stream)
+                   : launchPairTyped<kAMN, kBMN, Beta::kZero, false>(q, scratch, sms, device,
+                                                                      stream);
   if (q.beta == 1.0F)
-    return launchPairTyped<kAMN, kBMN, Beta::kOne>(q, scratch, sms, device, stream);
-  return launchPairTyped<kAMN, kBMN, Beta::kGeneral>(q, scratch, sms, device, stream);
+    return batched ? launchPairTyped<kAMN, kBMN, Beta::kOne, true>(q, scratch, sms, device, stream)
+                   : launchPairTyped<kAMN, kBMN, Beta::kOne, false>(q, scratch, sms, device,
+                                                                     stream);
+  return batched
+             ? launchPairTyped<kAMN, kBMN, Beta::kGeneral, true>(q, scratch, sms, device, stream)
+             : launchPairTyped<kAMN, kBMN, Beta::kGeneral, false>(q, scratch, sms, device, stream);
 }
 
 template <int kBN>
@@ -215,10 +229,10 @@ sgblasStatus_t launchSized(const kern::GemmParams &p, bool a_mn, bool b_mn, t::T
   const auto sw_mn = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   const unsigned long long lda_b = static_cast<unsigned long long>(p.lda) * 4;
   const unsigned long long ldb_b = static_cast<unsigned long long>(p.ldb) * 4;
-  const bool ok_a = a_mn ? encodeTiled2d(&q.tma_a, p.a, p.m, p.k, lda_b, 32, 32, sw_mn)
-                         : encodeTiled2d(&q.tma_a, p.a, p.k, p.m, lda_b, 32, t::kBM, sw_k);
-  const bool ok_b = b_mn ? encodeTiled2d(&q.tma_b, p.b, p.n, p.k, ldb_b, 32, 32, sw_mn)
-                         : encodeTiled2d(&q.tma_b, p.b, p.k, p.n, ldb_b, 32, kBN, sw_k);
+  const bool ok_a = a_mn ? encodeTiled3d(&q.tma_a, p.a, p.m, p.k, lda_b, p.batch, p.stride_a, 32, 32, sw_mn)
+                         : encodeTiled3d(&q.tma_a, p.a, p.k, p.m, lda_b, p.batch, p.stride_a, 32, t::kBM, sw_k);
+  const bool ok_b = b_mn ? encodeTiled3d(&q.tma_b, p.b, p.n, p.k, ldb_b, p.batch, p.stride_b, 32, 32, sw_mn)
+                         : encodeTiled3d(&q.tma_b, p.b, p.k, p.n, ldb_b, p.batch, p.stride_b, 32, kBN, sw_k);
   if (!ok_a || !ok_b) return SGBLAS_STATUS_EXECUTION_FAILED;
   if (a_mn && b_mn) return launchByBeta<kBN, true, true>(q, scratch, sms, device, stream);
   if (a_mn) return launchByBeta<kBN, true, false>(q, scratch, sms, device, stream);
@@ -232,6 +246,8 @@ sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, const Scr
                           int device, cudaStream_t stream) {
   t::Tf32Params q = {};
   q.c = p.c;
+  q.stride_c = p.stride_c;
+  q.batch = p.batch;
   q.m = p.m;
   q.n = p.n;
   q.k = p.k;
@@ -249,10 +265,10 @@ sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, const Scr
   // shorter estimated run, waves x tile time: a 128-wide tile takes 0.77 of a
   // 256-wide tile's time (measured: its operand traffic per FLOP is higher).
   auto waves = [&](long long bn) {
-    const long long tiles = static_cast<long long>(q.tiles_m) * ((p.n + bn - 1) / bn);
+    const long long tiles = static_cast<long long>(q.tiles_m) * ((p.n + bn - 1) / bn) * p.batch;
     return (tiles + sms - 1) / sms;
   };
-  if (static_cast<long long>(q.tiles_m) * ((p.n + 127) / 128) > INT_MAX)
+  if (static_cast<long long>(q.tiles_m) * ((p.n + 127) / 128) * p.batch > INT_MAX)
     return SGBLAS_STATUS_NOT_SUPPORTED;
   // A: op N keeps m contiguous (MN-major), op T keeps k contiguous (K-major);
   // B: op N keeps k contiguous (K-major), op T keeps n contiguous (MN-major).
@@ -260,14 +276,15 @@ sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, const Scr
   // Pair-CTA 256 x 256 tiles (half the B traffic per FLOP) once there is at
   // least one tile per pair; the stream-K rule balances a partial last wave.
   const int pairs = sms / 2;
-  const long long pair_tiles = static_cast<long long>((p.m + 255) / 256) * ((p.n + 255) / 256);
+  const long long pair_tiles =
+      static_cast<long long>((p.m + 255) / 256) * ((p.n + 255) / 256) * p.batch;
   if (pairs > 0 && pair_tiles >= pairs && pair_tiles <= INT_MAX) {
     if (a_mn && b_mn) return launchPair<true, true>(p, q, scratch, sms, device, stream);
     if (a_mn) return launchPair<true, false>(p, q, scratch, sms, device, stream);
     if (b_mn) return launchPair<false, true>(p, q, scratch, sms, device, stream);
     return launchPair<false, false>(p, q, scratch, sms, device, stream);
   }
-  const long long wide_tiles = static_cast<long long>(q.tiles_m) * ((p.n + 255) / 256);
+  const long long wide_tiles = static_cast<long long>(q.tiles_m) * ((p.n + 255) / 256) * p.batch;
   if (wide_tiles < sms && waves(128) * 77 < waves(256) * 100)
     return launchSized<128>(p, a_mn, b_mn, q, scratch, sms, device, stream);
   return launchSized<256>(p, a_mn, b_mn, q, scratch, sms, device, stream);

@@ -62,9 +62,14 @@ struct Cfg {
 };
 
 struct Tf32Params {
-  CUtensorMap tma_a;   // K-major: (k, m) boxes 32 x 128; MN-major: (m, k) boxes 32 x 32
-  CUtensorMap tma_b;   // K-major: (k, n) boxes 32 x N; MN-major: (n, k) boxes 32 x 32
+  // 3-D tensor maps, the third coordinate selecting the matrix of a strided
+  // batch. A: K-major (k, m) boxes 32 x 128; MN-major (m, k) boxes 32 x 32.
+  // B: K-major (k, n) boxes 32 x N; MN-major (n, k) boxes 32 x 32.
+  CUtensorMap tma_a;
+  CUtensorMap tma_b;
   float *c;
+  long long stride_c;   // C of matrix i at c + i * stride_c; tiles are batch-major
+  int batch;
   int m, n, k, ldc;
   float alpha, beta;
   int tiles_m, tiles_n, kiters, group_m;
@@ -106,7 +111,10 @@ __host__ __device__ constexpr uint32_t instrDesc() {
          (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 
-template <int kBN, bool kAMN, bool kBMN, Beta kBeta>
+// kBatch: tiles of a strided batch (p.batch > 1); the single-matrix
+// instantiation keeps the matrix index out of the epilogue, whose split-tile
+// fix-up runs at the edge of the register budget.
+template <int kBN, bool kAMN, bool kBMN, Beta kBeta, bool kBatch>
 __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant__ Tf32Params p) {
   using G = Cfg<kBN>;
   constexpr int kStages = G::kStages;
@@ -150,9 +158,11 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
   gridDependencyWait();
   allowDependentLaunch();
 
-  auto tileOrigin = [&](int tile, int *m0, int *n0) {
+  const int tiles_per_matrix = p.tiles_m * p.tiles_n;
+  auto tileOrigin = [&](int tile, int *m0, int *n0, int *bi) {
     int tm, tn;
-    rasterTile(p, tile, &tm, &tn);
+    *bi = kBatch ? tile / tiles_per_matrix : 0;
+    rasterTile(p, tile - *bi * tiles_per_matrix, &tm, &tn);
     *m0 = tm * kBM;
     *n0 = tn * kBN;
   };
@@ -167,8 +177,8 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
       int g = 0;  // k slices issued so far
       for (int i = 0; i < nitems; ++i) {
         const Item it = itemAt(p, cta, i);
-        int m0, n0;
-        tileOrigin(it.tile, &m0, &n0);
+        int m0, n0, bi;
+        tileOrigin(it.tile, &m0, &n0, &bi);
         for (int kb = it.kb; kb < it.ke; ++kb, ++g) {
           const int s = g % kStages;
           if (g >= kStages) wait(&empty[s], (g / kStages - 1) & 1);
@@ -178,15 +188,15 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
           mbarArriveExpectTx(&full[s], kStageBytes);
           if constexpr (kAMN) {
             for (int j = 0; j < kBM / 32; ++j)
-              tmaLoad2d(sa + j * kChunkBytes, &p.tma_a, &full[s], m0 + 32 * j, k0);
+              tmaLoad3d(sa + j * kChunkBytes, &p.tma_a, &full[s], m0 + 32 * j, k0, bi);
           } else {
-            tmaLoad2d(sa, &p.tma_a, &full[s], k0, m0);
+            tmaLoad3d(sa, &p.tma_a, &full[s], k0, m0, bi);
           }
           if constexpr (kBMN) {
             for (int j = 0; j < kBN / 32; ++j)
-              tmaLoad2d(sb + j * kChunkBytes, &p.tma_b, &full[s], n0 + 32 * j, k0);
+              tmaLoad3d(sb + j * kChunkBytes, &p.tma_b, &full[s], n0 + 32 * j, k0, bi);
           } else {
-            tmaLoad2d(sb, &p.tma_b, &full[s], k0, n0);
+            tmaLoad3d(sb, &p.tma_b, &full[s], k0, n0, bi);
           }
         }
       }
@@ -230,9 +240,9 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
     const int etid = threadIdx.x - 32 * kEpilogueWarp0;   // 0..127
     constexpr size_t kSlotFloats = static_cast<size_t>(kBM) * kBN;
     // C = alpha * acc + beta * C for 32 columns of this thread's row.
-    auto storeChunk = [&](int row, int col0, const float (&acc)[32]) {
+    auto storeChunk = [&](float *cbase, int row, int col0, const float (&acc)[32]) {
       const bool row_ok = row < p.m;
-      float *cp = p.c + static_cast<size_t>(col0) * p.ldc + row;
+      float *cp = cbase + static_cast<size_t>(col0) * p.ldc + row;
       float cv[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -249,8 +259,8 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
     for (int i = 0; i < nitems; ++i) {
       const Item it = itemAt(p, cta, i);
       const int b = i % kAccums;
-      int m0, n0;
-      tileOrigin(it.tile, &m0, &n0);
+      int m0, n0, bi;
+      tileOrigin(it.tile, &m0, &n0, &bi);
       wait(&acc_full[b], (i / kAccums) & 1);
       tcgenFenceAfter();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -263,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
           float acc[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(v[j]);
-          storeChunk(m0 + r, n0 + c * 32, acc);
+          storeChunk(kBatch ? p.c + bi * p.stride_c : p.c, m0 + r, n0 + c * 32, acc);
         }
         tcgenFenceBefore();
         mbarArrive(&acc_empty[b]);
@@ -342,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
               out[4 * q + 2] = acc[h * 8 + q].z;
               out[4 * q + 3] = acc[h * 8 + q].w;
             }
-            storeChunk(m0 + r, n0 + (c + h) * 32, out);
+            storeChunk(kBatch ? p.c + bi * p.stride_c : p.c, m0 + r, n0 + (c + h) * 32, out);
           }
         }
         if (etid == 0) p.counters[u] = 0;  // ready for the next launch
@@ -391,7 +401,7 @@ __host__ __device__ constexpr uint32_t instrDescPair() {
          (static_cast<uint32_t>(256 >> 4) << 24);
 }
 
-template <bool kAMN, bool kBMN, Beta kBeta>
+template <bool kAMN, bool kBMN, Beta kBeta, bool kBatch>
 __global__ void __launch_bounds__(kThreads, 1)
     tf32PairKernel(const __grid_constant__ Tf32Params p) {
   constexpr int kStages = Pair::kStages;
@@ -437,9 +447,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   gridDependencyWait();
   allowDependentLaunch();
 
-  auto tileOrigin = [&](int tile, int *m0, int *n0) {
+  const int tiles_per_matrix = p.tiles_m * p.tiles_n;
+  auto tileOrigin = [&](int tile, int *m0, int *n0, int *bi) {
     int tm, tn;
-    rasterTile(p, tile, &tm, &tn);
+    *bi = kBatch ? tile / tiles_per_matrix : 0;
+    rasterTile(p, tile - *bi * tiles_per_matrix, &tm, &tn);
     *m0 = tm * (2 * kBM);
     *n0 = tn * Pair::kBN;
   };
@@ -459,8 +471,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int g = 0;
       for (int i = 0; i < nitems; ++i) {
         const Item it = itemAt(p, pair, i);
-        int m0, n0;
-        tileOrigin(it.tile, &m0, &n0);
+        int m0, n0, bi;
+        tileOrigin(it.tile, &m0, &n0, &bi);
         const int am0 = m0 + static_cast<int>(rank) * kBM;
         const int bn0 = n0 + static_cast<int>(rank) * Pair::kBNHalf;
         for (int kb = it.kb; kb < it.ke; ++kb, ++g) {
@@ -473,15 +485,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (rank == 0) mbarArriveExpectTx(&full[s], 2 * kStageBytes);
           if constexpr (kAMN) {
             for (int j = 0; j < kBM / 32; ++j)
-              tmaLoad2dPair(sa + j * kChunkBytes, &p.tma_a, bar0, am0 + 32 * j, k0);
+              tmaLoad3dPair(sa + j * kChunkBytes, &p.tma_a, bar0, am0 + 32 * j, k0, bi);
           } else {
-            tmaLoad2dPair(sa, &p.tma_a, bar0, k0, am0);
+            tmaLoad3dPair(sa, &p.tma_a, bar0, k0, am0, bi);
           }
           if constexpr (kBMN) {
             for (int j = 0; j < Pair::kBNHalf / 32; ++j)
-              tmaLoad2dPair(sb + j * kChunkBytes, &p.tma_b, bar0, bn0 + 32 * j, k0);
+              tmaLoad3dPair(sb + j * kChunkBytes, &p.tma_b, bar0, bn0 + 32 * j, k0, bi);
           } else {
-            tmaLoad2dPair(sb, &p.tma_b, bar0, k0, bn0);
+            tmaLoad3dPair(sb, &p.tma_b, bar0, k0, bn0, bi);
           }
         }
       }
@@ -531,9 +543,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quarter * 32 + lane;
     const int etid = threadIdx.x - 32 * kEpilogueWarp0;   // 0..127
     constexpr size_t kSlotFloat4 = static_cast<size_t>(kBM) * Pair::kBN / 4;
-    auto storeChunk = [&](int row, int col0, const float (&acc)[32]) {
+    auto storeChunk = [&](float *cbase, int row, int col0, const float (&acc)[32]) {
       const bool row_ok = row < p.m;
-      float *cp = p.c + static_cast<size_t>(col0) * p.ldc + row;
+      float *cp = cbase + static_cast<size_t>(col0) * p.ldc + row;
       float cv[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -555,8 +567,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < nitems; ++i) {
       const Item it = itemAt(p, pair, i);
       const int b = i % kAccums;
-      int m0, n0;
-      tileOrigin(it.tile, &m0, &n0);
+      int m0, n0, bi;
+      tileOrigin(it.tile, &m0, &n0, &bi);
       wait(&acc_full[b], (i / kAccums) & 1);
       tcgenFenceAfter();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -570,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float acc[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(v[j]);
-          storeChunk(row, n0 + c * 32, acc);
+          storeChunk(kBatch ? p.c + bi * p.stride_c : p.c, row, n0 + c * 32, acc);
         }
         tcgenFenceBefore();
         mbarArriveCluster(clusterAddr(smemAddr(&acc_empty[b]), 0));
@@ -641,7 +653,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               out[4 * q + 2] = acc[h * 8 + q].z;
               out[4 * q + 3] = acc[h * 8 + q].w;
             }
-            storeChunk(row, n0 + (c + h) * 32, out);
+            storeChunk(kBatch ? p.c + bi * p.stride_c : p.c, row, n0 + (c + h) * 32, out);
           }
         }
         if (etid == 0) *counter = 0;  // ready for the next launch

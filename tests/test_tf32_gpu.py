@@ -122,8 +122,9 @@ def test_tf32_large_sampled(cuda, tf32_handle):
 
 
 def test_tf32_no_alloc_and_batched(cuda, tf32_handle):
-    """sgblasSgemmNoAlloc runs the TF32 lane without scratch; batched calls
-    in TF32 mode compute in FP32 (within the strict bound, which is tighter)."""
+    """sgblasSgemmNoAlloc runs the TF32 lane; a batch whose strides TMA
+    cannot use (here 0: one A and one B for every product) computes in FP32
+    (within the strict bound, which is tighter)."""
     torch = cuda
     case = C.Case("tf32-noalloc", 0, 1, 300, 260, 90, 300, 260, 300, 1.0, 0.0)
     a, b, c = C.cfg_inputs(case, 9, -1)
@@ -218,4 +219,34 @@ def test_tf32_pair_cta_stream_k(cuda, tf32_handle, ta, tb):
     cols = np.concatenate([rng.integers(0, n, 8192), rng.integers(0, n, m // 64)])
     ref, _ = oracle.sgemm_f64_points(ta, tb, k, 1.0, a, lda, b, ldb, 1.0, c, m, rows, cols)
     assert np.array_equal(out[rows + cols * m].astype(np.float64), ref)
+    assert sg.get_device_errors() == 0
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("m,n,k,count", [(300, 200, 70, 3), (1024, 1024, 96, 5)])
+def test_tf32_strided_batched(cuda, tf32_handle, ta, tb, m, n, k, count):
+    """Strided batches on the tensor cores (3-D tensor maps, batch-major
+    tiles): single-CTA tiles for the small batch, pair-CTA tiles for the
+    larger one. Integer inputs: every matrix exact."""
+    torch = cuda
+    lda, ldb, ldc = (k if ta else m) + 4, (n if tb else k) + 4, m + 2
+    sa = lda * (m if ta else k) + 8
+    sb = ldb * (k if tb else n) + 4
+    sc = ldc * n + 12
+    rng = np.random.default_rng(80 + m + 2 * ta + tb)
+    a = rng.integers(-2, 3, sa * count).astype(np.float32)
+    b = rng.integers(-2, 3, sb * count).astype(np.float32)
+    c = np.full(sc * count, np.nan, np.float32)
+    da = torch.from_numpy(a).cuda()
+    db = torch.from_numpy(b).cuda()
+    dc = torch.from_numpy(c).cuda()
+    tf32_handle.sgemm_strided_batched(ta, tb, m, n, k, 1.0, da, lda, sa, db, ldb, sb, 0.0, dc,
+                                      ldc, sc, count)
+    torch.cuda.synchronize()
+    out = dc.cpu().numpy()
+    for i in range(count):
+        ref, _ = oracle.sgemm_f64(ta, tb, m, n, k, 1.0, a[i * sa:(i + 1) * sa], lda,
+                                  b[i * sb:(i + 1) * sb], ldb, 0.0, c[i * sc:(i + 1) * sc], ldc)
+        got = c_view(out[i * sc:i * sc + ldc * n], m, n, ldc).astype(np.float64)
+        assert np.array_equal(got, ref), (i, ta, tb, m)
     assert sg.get_device_errors() == 0
