@@ -17,7 +17,9 @@ namespace {
 
 namespace t = kern::tf32;
 
-Schedule makeScheduleTf32(long long tiles, int kiters, int sms);
+// Shortest tile depth, in 32-deep k slices, whose partial last wave is split.
+constexpr int kMinTailSplitIters = 96;
+Schedule makeScheduleTf32(long long tiles, int kiters, int sms, bool batched);
 
 // Persistent schedule of `units` workers (CTAs, or CTA pairs) with the FP32
 // kernel's item structure and workspace layout ([counters | slots]), filled
@@ -31,7 +33,7 @@ Schedule makeScheduleTf32(long long tiles, int kiters, int sms);
 Schedule scheduleTf32(t::Tf32Params &q, long long tiles, int slots, int units,
                       const Scratch &scratch, int device, cudaStream_t stream,
                       bool *used_handle_workspace, int counters_per_tile = 1) {
-  Schedule s = makeScheduleTf32(tiles, q.kiters, units);
+  Schedule s = makeScheduleTf32(tiles, q.kiters, units, q.batch > 1);
   *used_handle_workspace = false;
   if (s.sk_tiles > 0) {
     const size_t need = kCounterRegionBytes + static_cast<size_t>(slots) * kSlotBytes;
@@ -69,14 +71,17 @@ Schedule scheduleTf32(t::Tf32Params &q, long long tiles, int slots, int units,
   return s;
 }
 
-Schedule makeScheduleTf32(long long tiles, int kiters, int sms) {
+Schedule makeScheduleTf32(long long tiles, int kiters, int sms, bool batched) {
   Schedule s;
   const int t = static_cast<int>(tiles);
   const bool splittable = kiters >= 2 * kMinSkIters;
+  // A tail split pays only for deep tiles (measured with pair tiles: k = 4096
+  // +3 %, k = 2048 -3 %), and not at all in the batched instantiation.
+  const bool tail_splittable = kiters >= kMinTailSplitIters && !batched;
   if (t >= sms) {
     const int rem = t % sms;
     s.grid = sms;
-    if (rem == 0 || 10 * rem >= 7 * sms || !splittable ||
+    if (rem == 0 || 10 * rem >= 7 * sms || !tail_splittable ||
         static_cast<long long>(rem) * kiters < static_cast<long long>(sms) * kMinSkIters) {
       s.dp_tiles = t;
     } else {

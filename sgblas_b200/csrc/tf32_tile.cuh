@@ -45,6 +45,9 @@ constexpr int kABytes = kBM * kBK * 4;        // 16 KiB
 constexpr int kChunkBytes = 32 * kBK * 4;     // one 32-wide MN chunk of an MN-major tile (4 KiB)
 constexpr int kThreads = 256;
 constexpr int kEpilogueWarp0 = 4;
+// Split-tile fix-up: 32-column chunks summed per pass (two pieces are loaded
+// per round trip to L2 in each pass).
+constexpr int kGatherChunks = 2;
 
 // Tile width N (UMMA N): 256, or 128 where the 256-wide tiles would leave a
 // poorly filled last wave. The stage ring fills about 192 KiB either way.
@@ -310,26 +313,26 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
           return reinterpret_cast<const float4 *>(p.ws) +
                  static_cast<size_t>(skSlot(p, pc, u)) * (kSlotFloats / 4);
         };
-        // Two chunks per pass, two pieces per round trip to L2 (the sum
-        // order per element stays piece order).
+        // kGatherChunks chunks per pass, two pieces per round trip to L2
+        // (the sum order per element stays piece order).
 #pragma unroll 1
-        for (int c = 0; c < kBN / 32; c += 2) {
-          float4 acc[16];
+        for (int c = 0; c < kBN / 32; c += kGatherChunks) {
+          float4 acc[8 * kGatherChunks];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) acc[e] = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+          for (int e = 0; e < 8 * kGatherChunks; ++e) acc[e] = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
 #pragma unroll 1
           for (int pc = first; pc <= last; pc += 2) {
             const bool two = pc + 1 <= last;
             const float4 *s0 = piece(pc) + c * 8 * kBM + r;
             const float4 *s1 = piece(two ? pc + 1 : pc) + c * 8 * kBM + r;
-            float4 v0[16], v1[16];
+            float4 v0[8 * kGatherChunks], v1[8 * kGatherChunks];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
+            for (int e = 0; e < 8 * kGatherChunks; ++e) {
               v0[e] = __ldcg(s0 + e * kBM);
               v1[e] = two ? __ldcg(s1 + e * kBM) : make_float4(0.0F, 0.0F, 0.0F, 0.0F);
             }
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
+            for (int e = 0; e < 8 * kGatherChunks; ++e) {
               acc[e].x += v0[e].x;
               acc[e].y += v0[e].y;
               acc[e].z += v0[e].z;
@@ -343,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
             }
           }
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
+          for (int h = 0; h < kGatherChunks; ++h) {
             float out[32];
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
@@ -614,23 +617,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (last_arrival) {
         __threadfence();
 #pragma unroll 1
-        for (int c = 0; c < Pair::kBN / 32; c += 2) {
-          float4 acc[16];
+        for (int c = 0; c < Pair::kBN / 32; c += kGatherChunks) {
+          float4 acc[8 * kGatherChunks];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) acc[e] = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
+          for (int e = 0; e < 8 * kGatherChunks; ++e) acc[e] = make_float4(0.0F, 0.0F, 0.0F, 0.0F);
 #pragma unroll 1
           for (int pc = first; pc <= last; pc += 2) {
             const bool two = pc + 1 <= last;
             const float4 *s0 = slotOf(pc, u) + c * 8 * kBM + r;
             const float4 *s1 = slotOf(two ? pc + 1 : pc, u) + c * 8 * kBM + r;
-            float4 v0[16], v1[16];
+            float4 v0[8 * kGatherChunks], v1[8 * kGatherChunks];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
+            for (int e = 0; e < 8 * kGatherChunks; ++e) {
               v0[e] = __ldcg(s0 + e * kBM);
               v1[e] = two ? __ldcg(s1 + e * kBM) : make_float4(0.0F, 0.0F, 0.0F, 0.0F);
             }
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
+            for (int e = 0; e < 8 * kGatherChunks; ++e) {
               acc[e].x += v0[e].x;
               acc[e].y += v0[e].y;
               acc[e].z += v0[e].z;
@@ -644,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
+          for (int h = 0; h < kGatherChunks; ++h) {
             float out[32];
 #pragma unroll
             for (int q = 0; q < 8; ++q) {

@@ -202,11 +202,11 @@ def test_tf32_pair_cta_tiles(cuda, tf32_handle, ta, tb):
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 def test_tf32_pair_cta_stream_k(cuda, tf32_handle, ta, tb):
-    """4096 x 4096: 256 pair tiles are 3.46 waves of 74 pairs, so the last
-    wave is split by k over all pairs (each CTA publishes and sums its half);
-    integer inputs: exact."""
+    """4096 x 4096 x 3072: 256 pair tiles are 3.46 waves of 74 pairs and deep
+    enough (96 slices of 32) for the last wave to be split by k over all
+    pairs (each CTA publishes and sums its half); integer inputs: exact."""
     torch = cuda
-    m, n, k = 4096, 4096, 320
+    m, n, k = 4096, 4096, 3072
     lda, ldb = (k if ta else m), (n if tb else k)
     rng = np.random.default_rng(60 + 2 * ta + tb)
     a = rng.integers(-2, 3, lda * (m if ta else k)).astype(np.float32)
