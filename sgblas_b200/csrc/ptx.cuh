@@ -212,7 +212,27 @@ __device__ __forceinline__ uint32_t clusterAddr(uint32_t local_smem, uint32_t ra
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem), "r"(rank));
   return r;
 }
-// Whole-cluster barrier (every thread of both CTAs), release / acquire.
+// This CTA's rank in its cluster, and the cluster's index along x.
+__device__ __forceinline__ uint32_t clusterRank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t clusterIdX() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+// 16-byte load from distributed shared memory (a cluster address).
+__device__ __forceinline__ float4 ldCluster4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+// Whole-cluster barrier (every thread of every CTA), release / acquire.
 __device__ __forceinline__ void clusterSync() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");

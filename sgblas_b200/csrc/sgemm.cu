@@ -2,9 +2,10 @@
 //
 // Entry-point semantics follow the reference CUDA build
 // (src/sgemm_cuda.cu:699-730 of AG0708/sgBLAS): NULL handle -> NOT_INITIALIZED;
-// validation errors as returned by validate(); no work -> SUCCESS; work in
-// TF32 mode -> NOT_SUPPORTED; otherwise enqueue on the handle's stream and
-// return without synchronizing. Unlike the reference, a launch clears only an
+// validation errors as returned by validate(); no work -> SUCCESS; otherwise
+// enqueue on the handle's stream and return without synchronizing (the
+// reference returns NOT_SUPPORTED for TF32 mode; here it selects the TF32
+// tensor-core lane). Unlike the reference, a launch clears only an
 // error it caused itself (cudaLaunchKernelEx returns the launch's own status),
 // so an error the caller left pending is not swallowed.
 #include "context.hpp"
@@ -343,6 +344,12 @@ sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOpe
   scratch.ctx = ctx;
 
   bool tA = ta == SGBLAS_OP_T, tB = tb == SGBLAS_OP_T;
+  // Small FP32 products: the cluster kernel, which stages any layout itself.
+  if (ctx->math_mode != SGBLAS_MATH_TF32) {
+    const int sms = smCount(device);
+    if (sms <= 0) return SGBLAS_STATUS_EXECUTION_FAILED;
+    if (smallEligible(p, sms)) return launchSmall(tA, tB, p, scratch, device, sms, stream);
+  }
   // An operand TMA cannot read in place (base not 16-byte aligned, or ld not
   // a multiple of 4 floats) is copied into the workspace as an x-contiguous
   // matrix (A: m x k, as for op N; B: n x k, as for op T) with an aligned

@@ -118,6 +118,20 @@ inline bool tf32Eligible(const float *a, int lda, const float *b, int ldb) {
 sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, const Scratch &scratch,
                           int device, cudaStream_t stream);
 
+// The small-problem kernel (sgemm_small.cu): 64 x 64 tiles of C, each computed
+// by one or more clusters of 1-8 CTAs that split its k range and sum their
+// partial tiles through distributed shared memory (and, with several
+// clusters per tile, through the stream-K scratch); any alignment, leading
+// dimension, transpose or batch form. Chosen when the persistent kernel's
+// 128 x 128 tiles number at most SMs / kSmallTileShare and each CTA of the
+// cluster kernel has at most kSmallMaxFmaPerCta multiply-adds.
+constexpr long long kSmallTileShare = 4;
+constexpr double kSmallMaxFmaPerCta = 2097152.0;   // 2^21 (512^3: 2^20 on 148 SMs)
+bool smallEligible(const kern::GemmParams &p, int sms);
+// p carries pointers, sizes, scalars and the batch (strides or arrays).
+sgblasStatus_t launchSmall(bool ta, bool tb, const kern::GemmParams &p, const Scratch &scratch,
+                           int device, int sms, cudaStream_t stream);
+
 // Launches one product of transpose mode (kTA, kTB). p carries the problem
 // (pointers, sizes, alpha, beta, error word); the launcher fills in the rest.
 template <bool kTA, bool kTB>

@@ -121,6 +121,11 @@ extern "C" sgblasStatus_t sgblasSgemmNoAlloc(sgblasHandle_t handle, sgblasOperat
   // accurate than TF32 asks).
   if (handle->math_mode == SGBLAS_MATH_TF32 && tf32Eligible(a, lda, b, ldb))
     return launchTf32(tA, tB, p, fixed, device, stream);
+  // Small products: the cluster kernel (scratch only when several clusters
+  // share a tile).
+  const int sms = smCount(device);
+  if (sms <= 0) return SGBLAS_STATUS_EXECUTION_FAILED;
+  if (smallEligible(p, sms)) return launchSmall(tA, tB, p, fixed, device, sms, stream);
   if (!tA && !tB) return launchMode<false, false>(p, fixed, device, stream);
   if (!tA && tB) return launchMode<false, true>(p, fixed, device, stream);
   if (tA && !tB) return launchMode<true, false>(p, fixed, device, stream);

@@ -1,0 +1,460 @@
+// The small-problem kernel: products too small to fill the GPU with the
+// persistent tile kernel's 128-row tiles (256^3, 512^3, a few small batched
+// matrices).
+//
+// Replaces the reference's small kernel family (64-row tiles,
+// src/sgemm_cuda.cu:598-640, sgemm_async_sm80_small.hpp) with a design for
+// 148 SMs:
+//   - C is cut into 64 x 64 tiles. Each tile belongs to one thread-block
+//     cluster of `split` CTAs (1, 2, 4 or 8) that divide its k range; split
+//     is the largest that keeps tiles x split within one CTA per SM, so a
+//     256^3 product runs on 128 SMs instead of 16.
+//   - Every CTA stages its k slices (32 deep) with 4-byte cp.async into a
+//     4-stage ring, any alignment, leading dimension or transpose, with zero
+//     fill outside the matrix; 256 threads each compute a 4 x 4 block of the
+//     tile with paired FMAs (fma.rn.f32x2), as the large kernel does.
+//   - The cluster's partial tiles are summed through distributed shared
+//     memory: CTA r reads its 1/split share of the tile from every CTA of the
+//     cluster in rank order (so results are deterministic), applies the
+//     alpha/beta epilogue and writes C. No workspace, counters or atomics:
+//     the kernel runs the same way from sgblasSgemm, sgblasSgemmNoAlloc and
+//     inside a CUDA graph.
+//   - Programmatic dependent launch: the prologue overlaps the previous
+//     kernel on the stream, and global memory is first read after
+//     griddepcontrol.wait.
+// Results obey the same bound as every other path (the reference's error
+// model: the k products are summed in FP32 in some order).
+#include "device.hpp"
+#include "ptx.cuh"
+#include "sgemm_launch.hpp"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <climits>
+#include <cstdint>
+
+namespace sgblas::kern::small {
+
+constexpr int kBM = 64;         // tile rows (m)
+constexpr int kBN = 64;         // tile columns (n)
+constexpr int kBK = 32;         // k slice per stage
+constexpr int kStages = 4;
+constexpr int kThreads = 256;
+constexpr int kRow = 68;        // floats per staged k row (64 + 4: no bank conflicts)
+constexpr int kTileFloats = kBK * kRow;
+constexpr int kStageFloats = 2 * kTileFloats;   // A and B
+constexpr int kSmemBytes = kStages * kStageFloats * 4;
+constexpr int kMaxSplit = 8;    // portable cluster size
+constexpr int kGroups = kBM * kBN / 4;          // float4 groups of one tile
+static_assert(kBN * kRow <= kStageFloats, "the partial tile fits in one stage");
+static_assert(kGroups % kThreads == 0, "whole groups per thread");
+
+struct Params {
+  const float *a, *b;
+  float *c;
+  const float *const *a_ptrs;   // pointer-array batches (else nullptr)
+  const float *const *b_ptrs;
+  float *const *c_ptrs;
+  long long stride_a, stride_b, stride_c;
+  int m, n, k, lda, ldb, ldc;
+  float alpha, beta;
+  int tiles_m;
+  int split;      // CTAs per cluster
+  int groups;     // clusters per tile
+  int slices;     // kBK slices of k
+  int per_cta;    // slices per CTA: CTA r of cluster g owns chunk g*split + r
+  int c_vec;      // C columns can be read and written as float4
+  float4 *ws;     // groups > 1: one partial tile per (tile, cluster)
+  int *counters;  // groups > 1: arrivals per (tile, rank), zero between launches
+};
+
+// Issues the copies of one operand's 64 x 32 slice into a [k][x] buffer
+// (row stride kRow). Element (x, k) of the operand is at src[x + k*ld]
+// (kKContig false) or src[k + x*ld] (kKContig true). Within a warp the
+// lanes read 32 consecutive floats (x-contiguous) or four runs of 8 (k-
+// contiguous), and write 32 different banks.
+template <bool kKContig>
+__device__ __forceinline__ void loadSlice(float *dst, const float *src, int ld, int x0, int xlim,
+                                          int k0, int klim, int tid) {
+#pragma unroll
+  for (int j = 0; j < kBM * kBK / kThreads; ++j) {
+    const int idx = tid + j * kThreads;
+    int xl, kl;
+    if constexpr (kKContig) {
+      const int lane = idx & 31, w = idx >> 5;
+      kl = (w & 3) * 8 + (lane & 7);
+      xl = (w >> 2) * 4 + (lane >> 3);
+    } else {
+      xl = idx & (kBM - 1);
+      kl = idx / kBM;
+    }
+    const int x = x0 + xl, kk = k0 + kl;
+    const bool ok = x < xlim && kk < klim;
+    const long long off = kKContig ? static_cast<long long>(x) * ld + kk
+                                   : static_cast<long long>(kk) * ld + x;
+    cpAsync4(dst + kl * kRow + xl, ok ? src + off : src, ok ? 4u : 0u);
+  }
+}
+
+template <Beta kBeta>
+__device__ __forceinline__ float4 loadC(const float *cp, int rows, bool vec) {
+  float4 v = make_float4(0.F, 0.F, 0.F, 0.F);
+  if constexpr (kBeta != Beta::kZero) {
+    if (vec && rows >= 4) {
+      v = *reinterpret_cast<const float4 *>(cp);
+    } else {
+      if (rows > 0) v.x = cp[0];
+      if (rows > 1) v.y = cp[1];
+      if (rows > 2) v.z = cp[2];
+      if (rows > 3) v.w = cp[3];
+    }
+  }
+  return v;
+}
+
+template <bool kTA, bool kTB, Beta kBeta>
+__global__ void __launch_bounds__(kThreads, 1) smallKernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(16) float smem[];
+  __shared__ int last_arrival;
+  const int tid = static_cast<int>(threadIdx.x);
+  const int split = p.split, groups = p.groups;
+  const int rank = static_cast<int>(clusterRank());
+  const int cluster = static_cast<int>(clusterIdX());
+  const int tile_m = cluster / groups, grp = cluster - tile_m * groups;
+  const int m0 = tile_m * kBM;
+  const int n0 = static_cast<int>(blockIdx.y) * kBN;
+  const int bi = static_cast<int>(blockIdx.z);
+  const int t0 = (grp * split + rank) * p.per_cta;
+  const int nt = max(0, min(p.slices - t0, p.per_cta));
+
+  gridDependencyWait();   // A, B, C (and pointer arrays) may come from the previous kernel
+  const float *A = p.a_ptrs != nullptr ? p.a_ptrs[bi] : p.a + bi * p.stride_a;
+  const float *B = p.b_ptrs != nullptr ? p.b_ptrs[bi] : p.b + bi * p.stride_b;
+  float *C = p.c_ptrs != nullptr ? p.c_ptrs[bi] : p.c + bi * p.stride_c;
+
+  auto load = [&](int stage, int t) {
+    float *as = smem + stage * kStageFloats;
+    const int k0 = t * kBK;
+    loadSlice<kTA>(as, A, p.lda, m0, p.m, k0, p.k, tid);                 // op(A)(m, k)
+    loadSlice<!kTB>(as + kTileFloats, B, p.ldb, n0, p.n, k0, p.k, tid);  // op(B)(k, n)
+  };
+
+  const int tx = tid & 15, ty = tid >> 4;   // the thread's 4 columns / 4 rows of the tile
+  float2 acc[4][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.F, 0.F);
+
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) {
+    if (s < nt) load(s, t0 + s);
+    cpAsyncCommit();
+  }
+  for (int i = 0; i < nt; ++i) {
+    cpAsyncWait<kStages - 2>();
+    __syncthreads();   // slice i landed; every thread is done with slice i - 1's stage
+    if (i + kStages - 1 < nt) load((i + kStages - 1) % kStages, t0 + i + kStages - 1);
+    cpAsyncCommit();
+    const float *as = smem + (i % kStages) * kStageFloats + ty * 4;
+    const float *bs = smem + (i % kStages) * kStageFloats + kTileFloats + tx * 4;
+    // Fragments of step kk + 1 are read while step kk computes.
+    float4 a = *reinterpret_cast<const float4 *>(as);
+    float4 b = *reinterpret_cast<const float4 *>(bs);
+#pragma unroll
+    for (int kk = 0; kk < kBK; ++kk) {
+      float4 an = a, bn = b;
+      if (kk + 1 < kBK) {
+        an = *reinterpret_cast<const float4 *>(as + (kk + 1) * kRow);
+        bn = *reinterpret_cast<const float4 *>(bs + (kk + 1) * kRow);
+      }
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float2 ar = make_float2(av[r], av[r]);
+        acc[r][0] = __ffma2_rn(ar, b01, acc[r][0]);
+        acc[r][1] = __ffma2_rn(ar, b23, acc[r][1]);
+      }
+      a = an;
+      b = bn;
+    }
+  }
+  cpAsyncWait<0>();
+  allowDependentLaunch();
+
+  // This CTA's share of the tile: float4 groups [lo, hi) in column-major
+  // order (group q holds rows 4*(q % 16) .. +3 of column q / 16).
+  const int lo = rank * kGroups / split, hi = (rank + 1) * kGroups / split;
+  constexpr int kPerThread = kGroups / kThreads;
+  auto rowsAt = [&](int q) { return p.m - (m0 + (q & 15) * 4); };
+  auto colAt = [&](int q) { return n0 + (q >> 4); };
+  auto cAt = [&](int q) {
+    return C + static_cast<long long>(colAt(q)) * p.ldc + m0 + (q & 15) * 4;
+  };
+  float4 cold[kPerThread];
+#pragma unroll
+  for (int u = 0; u < kPerThread; ++u) {
+    const int q = lo + tid + u * kThreads;
+    cold[u] = make_float4(0.F, 0.F, 0.F, 0.F);
+    if (groups == 1 && q < hi && rowsAt(q) > 0 && colAt(q) < p.n)
+      cold[u] = loadC<kBeta>(cAt(q), rowsAt(q), p.c_vec != 0);
+  }
+
+  // Partial tile, column-major with row stride kRow, in stage 0's space.
+  __syncthreads();   // every thread's last reads of the ring are done
+  float *part = smem;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 v = (j & 1) == 0 ? make_float4(acc[0][j >> 1].x, acc[1][j >> 1].x,
+                                                acc[2][j >> 1].x, acc[3][j >> 1].x)
+                                  : make_float4(acc[0][j >> 1].y, acc[1][j >> 1].y,
+                                                acc[2][j >> 1].y, acc[3][j >> 1].y);
+    *reinterpret_cast<float4 *>(part + (tx * 4 + j) * kRow + ty * 4) = v;
+  }
+  clusterSync();   // every CTA's partial tile is written and visible to the cluster
+
+  // The cluster's sum of this CTA's share, CTA by CTA in rank order.
+  const uint32_t part_addr = smemAddr(part);
+  float4 sum[kPerThread];
+#pragma unroll
+  for (int u = 0; u < kPerThread; ++u) {
+    const int q = lo + tid + u * kThreads;
+    sum[u] = make_float4(0.F, 0.F, 0.F, 0.F);
+    if (q >= hi) continue;
+    const uint32_t off = static_cast<uint32_t>((((q >> 4) * kRow) + (q & 15) * 4) * 4);
+    sum[u] = ldCluster4(clusterAddr(part_addr + off, 0));
+    for (int r = 1; r < split; ++r) {
+      const float4 v = ldCluster4(clusterAddr(part_addr + off, static_cast<uint32_t>(r)));
+      sum[u].x += v.x;
+      sum[u].y += v.y;
+      sum[u].z += v.z;
+      sum[u].w += v.w;
+    }
+  }
+  clusterSync();   // the other CTAs have read this CTA's partial tile
+
+  if (groups > 1) {
+    // Several clusters share the tile: each stores its sum, and for every
+    // share the last of them to arrive adds the stored sums in cluster
+    // order and writes C (same result whatever the arrival order).
+    const long long tile =
+        (static_cast<long long>(bi) * gridDim.y + blockIdx.y) * p.tiles_m + tile_m;
+    float4 *slots = p.ws + tile * groups * kGroups;
+#pragma unroll
+    for (int u = 0; u < kPerThread; ++u) {
+      const int q = lo + tid + u * kThreads;
+      if (q < hi) __stcg(slots + grp * kGroups + q, sum[u]);
+    }
+    __threadfence();
+    __syncthreads();
+    int *counter = p.counters + tile * split + rank;
+    if (tid == 0) last_arrival = atomicAdd(counter, 1) == groups - 1;
+    __syncthreads();
+    if (!last_arrival) return;
+    __threadfence();
+#pragma unroll
+    for (int u = 0; u < kPerThread; ++u) {
+      const int q = lo + tid + u * kThreads;
+      if (q >= hi) continue;
+      sum[u] = __ldcg(slots + q);
+      for (int g = 1; g < groups; ++g) {
+        const float4 v = __ldcg(slots + g * kGroups + q);
+        sum[u].x += v.x;
+        sum[u].y += v.y;
+        sum[u].z += v.z;
+        sum[u].w += v.w;
+      }
+      if (rowsAt(q) > 0 && colAt(q) < p.n)
+        cold[u] = loadC<kBeta>(cAt(q), rowsAt(q), p.c_vec != 0);
+    }
+    if (tid == 0) *counter = 0;   // every cluster of the tile has arrived
+  }
+
+  const float alpha = p.alpha, beta = p.beta;
+#pragma unroll
+  for (int u = 0; u < kPerThread; ++u) {
+    const int q = lo + tid + u * kThreads;
+    const int rows = rowsAt(q);
+    if (q >= hi || rows <= 0 || colAt(q) >= p.n) continue;
+    float *cp = cAt(q);
+    float4 out;
+    out.x = epilogueValue<kBeta>(sum[u].x, alpha, beta, cold[u].x);
+    out.y = epilogueValue<kBeta>(sum[u].y, alpha, beta, cold[u].y);
+    out.z = epilogueValue<kBeta>(sum[u].z, alpha, beta, cold[u].z);
+    out.w = epilogueValue<kBeta>(sum[u].w, alpha, beta, cold[u].w);
+    if (p.c_vec != 0 && rows >= 4) {
+      *reinterpret_cast<float4 *>(cp) = out;
+    } else {
+      cp[0] = out.x;
+      if (rows > 1) cp[1] = out.y;
+      if (rows > 2) cp[2] = out.z;
+      if (rows > 3) cp[3] = out.w;
+    }
+  }
+}
+
+}  // namespace sgblas::kern::small
+
+namespace sgblas::detail {
+
+namespace {
+
+using kern::Beta;
+namespace sm = kern::small;
+
+long long ceilDiv(long long a, long long b) { return (a + b - 1) / b; }
+
+template <bool kTA, bool kTB, Beta kBeta>
+sgblasStatus_t launchTyped(const sm::Params &p, dim3 grid, int device, cudaStream_t stream) {
+  auto kernel = sm::smallKernel<kTA, kTB, kBeta>;
+  static std::atomic<uint64_t> configured{0};
+  if (!configureKernel(reinterpret_cast<const void *>(kernel), device, sm::kSmemBytes,
+                       &configured))
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(sm::kThreads);
+  cfg.dynamicSmemBytes = sm::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2] = {};
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(p.split);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));
+}
+
+template <bool kTA, bool kTB>
+sgblasStatus_t launchByBeta(const sm::Params &p, dim3 grid, int device, cudaStream_t stream) {
+  if (p.beta == 0.0F) return launchTyped<kTA, kTB, Beta::kZero>(p, grid, device, stream);
+  if (p.beta == 1.0F) return launchTyped<kTA, kTB, Beta::kOne>(p, grid, device, stream);
+  return launchTyped<kTA, kTB, Beta::kGeneral>(p, grid, device, stream);
+}
+
+// CTAs per cluster: the largest power of two up to kMaxSplit that keeps one
+// CTA per SM and at least one k slice per CTA.
+int chooseSplit(long long tiles, int slices, int sms) {
+  int split = 1;
+  while (split * 2 <= sm::kMaxSplit && split * 2 <= slices && tiles * split * 2 <= sms)
+    split *= 2;
+  return split;
+}
+
+// Clusters per tile: more than one only when the tiles' clusters would
+// leave over half the SMs idle and k is deep enough to give every CTA
+// kMinSlicesPerCta slices.
+constexpr int kMinSlicesPerCta = 4;
+int chooseGroups(long long tiles, int split, int slices, int sms) {
+  const long long ctas = tiles * split;
+  if (ctas * 2 > sms) return 1;
+  const long long by_sms = sms / ctas;
+  const long long by_k = slices / (static_cast<long long>(split) * kMinSlicesPerCta);
+  return static_cast<int>(std::max(1LL, std::min(by_sms, by_k)));
+}
+
+struct SmallPlan {
+  long long tiles_m, tiles_n, tiles;
+  int slices, split, groups;
+};
+
+SmallPlan planSmall(const kern::GemmParams &p, int sms) {
+  SmallPlan s;
+  s.tiles_m = ceilDiv(p.m, sm::kBM);
+  s.tiles_n = ceilDiv(p.n, sm::kBN);
+  s.tiles = s.tiles_m * s.tiles_n * p.batch;
+  s.slices = static_cast<int>(ceilDiv(p.k, sm::kBK));
+  s.split = chooseSplit(s.tiles, s.slices, sms);
+  s.groups = chooseGroups(s.tiles, s.split, s.slices, sms);
+  return s;
+}
+
+}  // namespace
+
+bool smallEligible(const kern::GemmParams &p, int sms) {
+  const long long tiles_m = ceilDiv(p.m, sm::kBM), tiles_n = ceilDiv(p.n, sm::kBN);
+  if (p.batch > 65535 || tiles_n > 65535 || tiles_m * sm::kMaxSplit * sms > INT_MAX) return false;
+  // The persistent kernel's 128 x 128 tiles would leave most SMs without a
+  // whole tile, and each CTA here has little enough work that latency, not
+  // FMA throughput, decides the time.
+  const long long tiles128 = ceilDiv(p.m, 128) * ceilDiv(p.n, 128) * p.batch;
+  if (tiles128 * kSmallTileShare > sms) return false;
+  const SmallPlan s = planSmall(p, sms);
+  const double fma_per_cta = static_cast<double>(p.m) * p.n * p.k * p.batch /
+                             (static_cast<double>(s.tiles) * s.split * s.groups);
+  return fma_per_cta <= kSmallMaxFmaPerCta;
+}
+
+sgblasStatus_t launchSmall(bool ta, bool tb, const kern::GemmParams &gp, const Scratch &scratch,
+                           int device, int sms, cudaStream_t stream) {
+  sm::Params p = {};
+  p.a = gp.a;
+  p.b = gp.b;
+  p.c = gp.c;
+  p.a_ptrs = gp.a_ptrs;
+  p.b_ptrs = gp.b_ptrs;
+  p.c_ptrs = gp.c_ptrs;
+  p.stride_a = gp.batch > 1 ? gp.stride_a : 0;
+  p.stride_b = gp.batch > 1 ? gp.stride_b : 0;
+  p.stride_c = gp.batch > 1 ? gp.stride_c : 0;
+  p.m = gp.m;
+  p.n = gp.n;
+  p.k = gp.k;
+  p.lda = gp.lda;
+  p.ldb = gp.ldb;
+  p.ldc = gp.ldc;
+  p.alpha = gp.alpha;
+  p.beta = gp.beta;
+  const SmallPlan s = planSmall(gp, sms);
+  p.tiles_m = static_cast<int>(s.tiles_m);
+  p.slices = s.slices;
+  p.split = s.split;
+  p.groups = s.groups;
+  bool used_handle_workspace = false;
+  if (p.groups > 1) {
+    // [arrival counters | one partial tile per (tile, cluster)], the layout
+    // of the tile kernel's stream-K scratch; without it, one cluster per tile.
+    const size_t counters = static_cast<size_t>(s.tiles) * s.split;
+    const size_t need = kCounterRegionBytes +
+                        static_cast<size_t>(s.tiles) * p.groups * sm::kGroups * sizeof(float4);
+    unsigned char *base = nullptr;
+    if (counters * sizeof(int) > kCounterRegionBytes) {
+      base = nullptr;
+    } else if (scratch.fixed != nullptr) {
+      if (need <= scratch.fixed_bytes) {
+        if (cudaMemsetAsync(scratch.fixed, 0, counters * sizeof(int), stream) != cudaSuccess)
+          return launchStatus(cudaErrorUnknown);
+        base = scratch.fixed;
+      }
+    } else if (ensureWorkspace(scratch.ctx, need, device, stream)) {
+      base = static_cast<unsigned char *>(scratch.ctx->workspace);
+      used_handle_workspace = true;
+    }
+    if (base != nullptr) {
+      p.counters = reinterpret_cast<int *>(base);
+      p.ws = reinterpret_cast<float4 *>(base + kCounterRegionBytes);
+    } else {
+      p.groups = 1;
+    }
+  }
+  p.per_cta = static_cast<int>(ceilDiv(p.slices, static_cast<long long>(p.split) * p.groups));
+  p.c_vec = gp.c_ptrs == nullptr && aligned16(gp.c) && p.ldc % 4 == 0 &&
+            (gp.batch == 1 || gp.stride_c % 4 == 0);
+  const dim3 grid(static_cast<unsigned>(s.tiles_m * p.groups * p.split),
+                  static_cast<unsigned>(s.tiles_n), static_cast<unsigned>(gp.batch));
+  sgblasStatus_t st;
+  if (!ta && !tb) st = launchByBeta<false, false>(p, grid, device, stream);
+  else if (!ta && tb) st = launchByBeta<false, true>(p, grid, device, stream);
+  else if (ta && !tb) st = launchByBeta<true, false>(p, grid, device, stream);
+  else st = launchByBeta<true, true>(p, grid, device, stream);
+  if (st == SGBLAS_STATUS_SUCCESS && used_handle_workspace &&
+      !markWorkspaceUse(scratch.ctx, stream))
+    return SGBLAS_STATUS_EXECUTION_FAILED;
+  return st;
+}
+
+}  // namespace sgblas::detail

@@ -55,8 +55,12 @@ STRIDED = []
 for ta in (0, 1):
     for tb in (0, 1):
         # (m, n, k, pad, extra stride floats): extra % 4 == 0 keeps TMA
+        # small-problem cluster kernel (at most 37 tiles of 128 x 128) ...
         STRIDED.append((ta, tb, 300, 200, 70, 0, 8))
         STRIDED.append((ta, tb, 257, 129, 33, 4, 3))
+        # ... and the persistent tile kernel
+        STRIDED.append((ta, tb, 700, 600, 70, 0, 8))
+        STRIDED.append((ta, tb, 650, 520, 33, 4, 3))
 STRIDED += [(0, 0, 1000, 700, 900, 0, 0), (1, 0, 129, 1031, 400, 4, 4)]
 
 
@@ -82,12 +86,13 @@ def test_strided_batched(cuda, handle, ta, tb, m, n, k, pad, extra):
     assert sg.get_device_errors() == 0
 
 
+@pytest.mark.parametrize("m,n", [(260, 190), (1000, 700)])
 @pytest.mark.parametrize("stride_sign", [0, -1])
-def test_strided_batched_reuse_and_negative_strides(cuda, handle, stride_sign):
+def test_strided_batched_reuse_and_negative_strides(cuda, handle, stride_sign, m, n):
     """stride_a == 0 reuses one A for every product; negative strides walk
-    the batch backwards from the base pointer."""
+    the batch backwards from the base pointer (small and tile kernels)."""
     torch = cuda
-    count, m, n, k = 4, 260, 190, 150
+    count, k = 4, 150
     case = C.Case("reuse", 0, 1, m, n, k, m, n, m, 1.5, 0.5)
     mats = _matrices(case, count, 77)
     a_shared = mats[0][0]
@@ -106,11 +111,13 @@ def test_strided_batched_reuse_and_negative_strides(cuda, handle, stride_sign):
         _check(case, a_shared, b, c, got, (stride_sign, i))
 
 
+@pytest.mark.parametrize("m,n", [(231, 300), (700, 600)])
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
-def test_pointer_array_batched(cuda, handle, ta, tb):
-    """Device arrays of pointers, in shuffled order, one matrix misaligned."""
+def test_pointer_array_batched(cuda, handle, ta, tb, m, n):
+    """Device arrays of pointers, in shuffled order, one matrix misaligned
+    (small and tile kernels)."""
     torch = cuda
-    count, m, n, k = 5, 231, 300, 97
+    count, k = 5, 97
     case = C.Case("arrays", ta, tb, m, n, k, (k if ta else m) + 1, (n if tb else k) + 2, m + 3,
                   -0.5, 2.0)
     mats = _matrices(case, count, 901)

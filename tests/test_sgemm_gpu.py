@@ -110,10 +110,14 @@ def test_cfg4_medium_skinny(cuda, handle, shape):
 
 
 # ---- loader paths, tails, leading dimensions, alignment -----------------------
+# The first five shapes run on the small-problem cluster kernel, the last four
+# (more than 37 tiles of 128 x 128) on the persistent tile kernel's loaders.
+PATH_SHAPES = ((300, 200, 70), (257, 129, 33), (1, 1, 1), (5, 300, 17), (511, 3, 1),
+               (1300, 1000, 70), (1029, 1157, 33), (1, 9000, 17), (9001, 3, 1))
 PATH_CASES = []
 for ta in (0, 1):
     for tb in (0, 1):
-        for (m, n, k) in ((300, 200, 70), (257, 129, 33), (1, 1, 1), (5, 300, 17), (511, 3, 1)):
+        for (m, n, k) in PATH_SHAPES:
             for pad, offs in ((0, (0, 0, 0)), (4, (0, 0, 0)), (1, (0, 0, 0)), (0, (1, 2, 3))):
                 PATH_CASES.append((ta, tb, m, n, k, pad, offs))
 
@@ -134,11 +138,12 @@ def test_paths_tails_alignment(cuda, handle, ta, tb, m, n, k, pad, offs):
 
 # Without a workspace (sgblasSgemmNoAlloc) an operand TMA cannot read is
 # staged by the tile kernel's cp.async producer in 4-, 8- or 16-byte copies
-# instead of being copied into the workspace first: cover those paths too.
+# instead of being copied into the workspace first: cover those paths too
+# (shapes large enough for the tile kernel).
 COPY_CASES = []
 for ta in (0, 1):
     for tb in (0, 1):
-        for (m, n, k) in ((300, 200, 70), (257, 129, 33), (5, 300, 17)):
+        for (m, n, k) in ((1300, 1000, 70), (1029, 1157, 33), (5, 9000, 17)):
             for pad, offs in ((1, (0, 0, 0)), (2, (0, 0, 0)), (0, (1, 2, 3)), (4, (2, 0, 1))):
                 COPY_CASES.append((ta, tb, m, n, k, pad, offs))
 
