@@ -37,19 +37,29 @@
 
 namespace sgblas::kern::small {
 
-constexpr int kBM = 64;         // tile rows (m)
 constexpr int kBN = 64;         // tile columns (n)
 constexpr int kBK = 32;         // k slice per stage
 constexpr int kStages = 4;
-constexpr int kThreads = 256;
-constexpr int kRow = 68;        // floats per staged k row (64 + 4: no bank conflicts)
-constexpr int kTileFloats = kBK * kRow;
-constexpr int kStageFloats = 2 * kTileFloats;   // A and B
-constexpr int kSmemBytes = kStages * kStageFloats * 4;
+constexpr int kThreads = 256;   // a 16 x 16 grid of threads over the tile
+constexpr int kTN = kBN / 16;   // columns per thread
+constexpr int kRowB = kBN + 4;  // floats per staged k row (padding: no bank conflicts)
 constexpr int kMaxSplit = 8;    // portable cluster size
-constexpr int kGroups = kBM * kBN / 4;          // float4 groups of one tile
-static_assert(kBN * kRow <= kStageFloats, "the partial tile fits in one stage");
-static_assert(kGroups % kThreads == 0, "whole groups per thread");
+static_assert(kTN == 4, "4 columns per thread");
+
+// Tiles of kBM (64 or 128) rows x kBN columns.
+template <int kBM>
+struct Tile {
+  static constexpr int kTM = kBM / 16;       // rows per thread
+  static constexpr int kRowA = kBM + 4;
+  static constexpr int kTileA = kBK * kRowA;
+  static constexpr int kStageFloats = kTileA + kBK * kRowB;
+  static constexpr int kSmemBytes = kStages * kStageFloats * 4;
+  static constexpr int kColGroups = kBM / 4;  // float4 groups per tile column
+  static constexpr int kGroups = kBM * kBN / 4;
+  static_assert(kTM % 4 == 0, "whole float4s of rows per thread");
+  static_assert(kBN * kRowA <= kStages * kStageFloats, "the partial tile fits in the ring");
+  static_assert(kGroups % kThreads == 0, "whole groups per thread");
+};
 
 struct Params {
   const float *a, *b;
@@ -70,16 +80,17 @@ struct Params {
   int *counters;  // groups > 1: arrivals per (tile, rank), zero between launches
 };
 
-// Issues the copies of one operand's 64 x 32 slice into a [k][x] buffer
-// (row stride kRow). Element (x, k) of the operand is at src[x + k*ld]
+// Issues the copies of one operand's kX x kBK slice into a [k][x] buffer
+// (row stride kX + 4). Element (x, k) of the operand is at src[x + k*ld]
 // (kKContig false) or src[k + x*ld] (kKContig true). Within a warp the
 // lanes read 32 consecutive floats (x-contiguous) or four runs of 8 (k-
 // contiguous), and write 32 different banks.
-template <bool kKContig>
+template <int kX, bool kKContig>
 __device__ __forceinline__ void loadSlice(float *dst, const float *src, int ld, int x0, int xlim,
                                           int k0, int klim, int tid) {
+  constexpr int kRow = kX + 4;
 #pragma unroll
-  for (int j = 0; j < kBM * kBK / kThreads; ++j) {
+  for (int j = 0; j < kX * kBK / kThreads; ++j) {
     const int idx = tid + j * kThreads;
     int xl, kl;
     if constexpr (kKContig) {
@@ -87,8 +98,8 @@ __device__ __forceinline__ void loadSlice(float *dst, const float *src, int ld, 
       kl = (w & 3) * 8 + (lane & 7);
       xl = (w >> 2) * 4 + (lane >> 3);
     } else {
-      xl = idx & (kBM - 1);
-      kl = idx / kBM;
+      xl = idx & (kX - 1);
+      kl = idx / kX;
     }
     const int x = x0 + xl, kk = k0 + kl;
     const bool ok = x < xlim && kk < klim;
@@ -114,8 +125,12 @@ __device__ __forceinline__ float4 loadC(const float *cp, int rows, bool vec) {
   return v;
 }
 
-template <bool kTA, bool kTB, Beta kBeta>
+template <int kBM, bool kTA, bool kTB, Beta kBeta>
 __global__ void __launch_bounds__(kThreads, 1) smallKernel(const __grid_constant__ Params p) {
+  using T = Tile<kBM>;
+  constexpr int kTM = T::kTM, kRowA = T::kRowA, kTileA = T::kTileA;
+  constexpr int kStageFloats = T::kStageFloats, kColGroups = T::kColGroups;
+  constexpr int kGroups = T::kGroups;
   extern __shared__ __align__(16) float smem[];
   __shared__ int last_arrival;
   const int tid = static_cast<int>(threadIdx.x);
@@ -137,14 +152,14 @@ __global__ void __launch_bounds__(kThreads, 1) smallKernel(const __grid_constant
   auto load = [&](int stage, int t) {
     float *as = smem + stage * kStageFloats;
     const int k0 = t * kBK;
-    loadSlice<kTA>(as, A, p.lda, m0, p.m, k0, p.k, tid);                 // op(A)(m, k)
-    loadSlice<!kTB>(as + kTileFloats, B, p.ldb, n0, p.n, k0, p.k, tid);  // op(B)(k, n)
+    loadSlice<kBM, kTA>(as, A, p.lda, m0, p.m, k0, p.k, tid);             // op(A)(m, k)
+    loadSlice<kBN, !kTB>(as + kTileA, B, p.ldb, n0, p.n, k0, p.k, tid);   // op(B)(k, n)
   };
 
-  const int tx = tid & 15, ty = tid >> 4;   // the thread's 4 columns / 4 rows of the tile
-  float2 acc[4][2];
+  const int tx = tid & 15, ty = tid >> 4;   // the thread's kTN columns / kTM rows of the tile
+  float2 acc[kTM][kTN / 2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.F, 0.F);
+  for (int i = 0; i < kTM; ++i) acc[i][0] = acc[i][1] = make_float2(0.F, 0.F);
 
 #pragma unroll
   for (int s = 0; s < kStages - 1; ++s) {
@@ -156,27 +171,37 @@ __global__ void __launch_bounds__(kThreads, 1) smallKernel(const __grid_constant
     __syncthreads();   // slice i landed; every thread is done with slice i - 1's stage
     if (i + kStages - 1 < nt) load((i + kStages - 1) % kStages, t0 + i + kStages - 1);
     cpAsyncCommit();
-    const float *as = smem + (i % kStages) * kStageFloats + ty * 4;
-    const float *bs = smem + (i % kStages) * kStageFloats + kTileFloats + tx * 4;
+    const float *as = smem + (i % kStages) * kStageFloats + ty * kTM;
+    const float *bs = smem + (i % kStages) * kStageFloats + kTileA + tx * kTN;
     // Fragments of step kk + 1 are read while step kk computes.
-    float4 a = *reinterpret_cast<const float4 *>(as);
-    float4 b = *reinterpret_cast<const float4 *>(bs);
+    float4 a[kTM / 4], b;
+#pragma unroll
+    for (int v = 0; v < kTM / 4; ++v) a[v] = *reinterpret_cast<const float4 *>(as + 4 * v);
+    b = *reinterpret_cast<const float4 *>(bs);
 #pragma unroll
     for (int kk = 0; kk < kBK; ++kk) {
-      float4 an = a, bn = b;
+      float4 an[kTM / 4], bn = b;
+#pragma unroll
+      for (int v = 0; v < kTM / 4; ++v) an[v] = a[v];
       if (kk + 1 < kBK) {
-        an = *reinterpret_cast<const float4 *>(as + (kk + 1) * kRow);
-        bn = *reinterpret_cast<const float4 *>(bs + (kk + 1) * kRow);
+#pragma unroll
+        for (int v = 0; v < kTM / 4; ++v)
+          an[v] = *reinterpret_cast<const float4 *>(as + (kk + 1) * kRowA + 4 * v);
+        bn = *reinterpret_cast<const float4 *>(bs + (kk + 1) * kRowB);
       }
-      const float av[4] = {a.x, a.y, a.z, a.w};
       const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const float2 ar = make_float2(av[r], av[r]);
-        acc[r][0] = __ffma2_rn(ar, b01, acc[r][0]);
-        acc[r][1] = __ffma2_rn(ar, b23, acc[r][1]);
+      for (int v = 0; v < kTM / 4; ++v) {
+        const float av[4] = {a[v].x, a[v].y, a[v].z, a[v].w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const float2 ar = make_float2(av[r], av[r]);
+          acc[4 * v + r][0] = __ffma2_rn(ar, b01, acc[4 * v + r][0]);
+          acc[4 * v + r][1] = __ffma2_rn(ar, b23, acc[4 * v + r][1]);
+        }
       }
-      a = an;
+#pragma unroll
+      for (int v = 0; v < kTM / 4; ++v) a[v] = an[v];
       b = bn;
     }
   }
@@ -184,13 +209,14 @@ __global__ void __launch_bounds__(kThreads, 1) smallKernel(const __grid_constant
   allowDependentLaunch();
 
   // This CTA's share of the tile: float4 groups [lo, hi) in column-major
-  // order (group q holds rows 4*(q % 16) .. +3 of column q / 16).
+  // order (group q holds rows 4*(q % kColGroups) .. +3 of column
+  // q / kColGroups).
   const int lo = rank * kGroups / split, hi = (rank + 1) * kGroups / split;
   constexpr int kPerThread = kGroups / kThreads;
-  auto rowsAt = [&](int q) { return p.m - (m0 + (q & 15) * 4); };
-  auto colAt = [&](int q) { return n0 + (q >> 4); };
+  auto rowsAt = [&](int q) { return p.m - (m0 + (q % kColGroups) * 4); };
+  auto colAt = [&](int q) { return n0 + q / kColGroups; };
   auto cAt = [&](int q) {
-    return C + static_cast<long long>(colAt(q)) * p.ldc + m0 + (q & 15) * 4;
+    return C + static_cast<long long>(colAt(q)) * p.ldc + m0 + (q % kColGroups) * 4;
   };
   float4 cold[kPerThread];
 #pragma unroll
@@ -201,16 +227,21 @@ __global__ void __launch_bounds__(kThreads, 1) smallKernel(const __grid_constant
       cold[u] = loadC<kBeta>(cAt(q), rowsAt(q), p.c_vec != 0);
   }
 
-  // Partial tile, column-major with row stride kRow, in stage 0's space.
+  // Partial tile, column-major with row stride kRowA, over the ring.
   __syncthreads();   // every thread's last reads of the ring are done
   float *part = smem;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float4 v = (j & 1) == 0 ? make_float4(acc[0][j >> 1].x, acc[1][j >> 1].x,
-                                                acc[2][j >> 1].x, acc[3][j >> 1].x)
-                                  : make_float4(acc[0][j >> 1].y, acc[1][j >> 1].y,
-                                                acc[2][j >> 1].y, acc[3][j >> 1].y);
-    *reinterpret_cast<float4 *>(part + (tx * 4 + j) * kRow + ty * 4) = v;
+  for (int j = 0; j < kTN; ++j) {
+#pragma unroll
+    for (int v = 0; v < kTM / 4; ++v) {
+      const float4 val =
+          (j & 1) == 0
+              ? make_float4(acc[4 * v][j >> 1].x, acc[4 * v + 1][j >> 1].x,
+                            acc[4 * v + 2][j >> 1].x, acc[4 * v + 3][j >> 1].x)
+              : make_float4(acc[4 * v][j >> 1].y, acc[4 * v + 1][j >> 1].y,
+                            acc[4 * v + 2][j >> 1].y, acc[4 * v + 3][j >> 1].y);
+      *reinterpret_cast<float4 *>(part + (tx * kTN + j) * kRowA + ty * kTM + 4 * v) = val;
+    }
   }
   clusterSync();   // every CTA's partial tile is written and visible to the cluster
 
@@ -222,14 +253,22 @@ __global__ void __launch_bounds__(kThreads, 1) smallKernel(const __grid_constant
     const int q = lo + tid + u * kThreads;
     sum[u] = make_float4(0.F, 0.F, 0.F, 0.F);
     if (q >= hi) continue;
-    const uint32_t off = static_cast<uint32_t>((((q >> 4) * kRow) + (q & 15) * 4) * 4);
-    sum[u] = ldCluster4(clusterAddr(part_addr + off, 0));
-    for (int r = 1; r < split; ++r) {
-      const float4 v = ldCluster4(clusterAddr(part_addr + off, static_cast<uint32_t>(r)));
-      sum[u].x += v.x;
-      sum[u].y += v.y;
-      sum[u].z += v.z;
-      sum[u].w += v.w;
+    const uint32_t off =
+        static_cast<uint32_t>(((q / kColGroups) * kRowA + (q % kColGroups) * 4) * 4);
+    // All of the cluster's reads are issued before the first add.
+    float4 v[kMaxSplit];
+#pragma unroll
+    for (int r = 0; r < kMaxSplit; ++r)
+      if (r < split) v[r] = ldCluster4(clusterAddr(part_addr + off, static_cast<uint32_t>(r)));
+    sum[u] = v[0];
+#pragma unroll
+    for (int r = 1; r < kMaxSplit; ++r) {
+      if (r < split) {
+        sum[u].x += v[r].x;
+        sum[u].y += v[r].y;
+        sum[u].z += v[r].z;
+        sum[u].w += v[r].w;
+      }
     }
   }
   clusterSync();   // the other CTAs have read this CTA's partial tile
@@ -305,17 +344,17 @@ namespace sm = kern::small;
 
 long long ceilDiv(long long a, long long b) { return (a + b - 1) / b; }
 
-template <bool kTA, bool kTB, Beta kBeta>
+template <int kBM, bool kTA, bool kTB, Beta kBeta>
 sgblasStatus_t launchTyped(const sm::Params &p, dim3 grid, int device, cudaStream_t stream) {
-  auto kernel = sm::smallKernel<kTA, kTB, kBeta>;
+  auto kernel = sm::smallKernel<kBM, kTA, kTB, kBeta>;
+  constexpr int kSmem = sm::Tile<kBM>::kSmemBytes;
   static std::atomic<uint64_t> configured{0};
-  if (!configureKernel(reinterpret_cast<const void *>(kernel), device, sm::kSmemBytes,
-                       &configured))
+  if (!configureKernel(reinterpret_cast<const void *>(kernel), device, kSmem, &configured))
     return SGBLAS_STATUS_EXECUTION_FAILED;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(sm::kThreads);
-  cfg.dynamicSmemBytes = sm::kSmemBytes;
+  cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2] = {};
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -329,11 +368,20 @@ sgblasStatus_t launchTyped(const sm::Params &p, dim3 grid, int device, cudaStrea
   return launchStatus(cudaLaunchKernelEx(&cfg, kernel, p));
 }
 
-template <bool kTA, bool kTB>
+template <int kBM, bool kTA, bool kTB>
 sgblasStatus_t launchByBeta(const sm::Params &p, dim3 grid, int device, cudaStream_t stream) {
-  if (p.beta == 0.0F) return launchTyped<kTA, kTB, Beta::kZero>(p, grid, device, stream);
-  if (p.beta == 1.0F) return launchTyped<kTA, kTB, Beta::kOne>(p, grid, device, stream);
-  return launchTyped<kTA, kTB, Beta::kGeneral>(p, grid, device, stream);
+  if (p.beta == 0.0F) return launchTyped<kBM, kTA, kTB, Beta::kZero>(p, grid, device, stream);
+  if (p.beta == 1.0F) return launchTyped<kBM, kTA, kTB, Beta::kOne>(p, grid, device, stream);
+  return launchTyped<kBM, kTA, kTB, Beta::kGeneral>(p, grid, device, stream);
+}
+
+template <int kBM>
+sgblasStatus_t launchByMode(bool ta, bool tb, const sm::Params &p, dim3 grid, int device,
+                            cudaStream_t stream) {
+  if (!ta && !tb) return launchByBeta<kBM, false, false>(p, grid, device, stream);
+  if (!ta && tb) return launchByBeta<kBM, false, true>(p, grid, device, stream);
+  if (ta && !tb) return launchByBeta<kBM, true, false>(p, grid, device, stream);
+  return launchByBeta<kBM, true, true>(p, grid, device, stream);
 }
 
 // CTAs per cluster: the largest power of two up to kMaxSplit that keeps one
@@ -358,34 +406,53 @@ int chooseGroups(long long tiles, int split, int slices, int sms) {
 }
 
 struct SmallPlan {
+  int bm;   // tile rows: 64 or 128
   long long tiles_m, tiles_n, tiles;
-  int slices, split, groups;
+  int slices, split, groups, per_cta;
+  long long ctas() const { return tiles * split * groups; }
 };
 
-SmallPlan planSmall(const kern::GemmParams &p, int sms) {
+SmallPlan planFor(const kern::GemmParams &p, int sms, int bm) {
   SmallPlan s;
-  s.tiles_m = ceilDiv(p.m, sm::kBM);
+  s.bm = bm;
+  s.tiles_m = ceilDiv(p.m, bm);
   s.tiles_n = ceilDiv(p.n, sm::kBN);
   s.tiles = s.tiles_m * s.tiles_n * p.batch;
   s.slices = static_cast<int>(ceilDiv(p.k, sm::kBK));
   s.split = chooseSplit(s.tiles, s.slices, sms);
   s.groups = chooseGroups(s.tiles, s.split, s.slices, sms);
+  s.per_cta = static_cast<int>(ceilDiv(s.slices, static_cast<long long>(s.split) * s.groups));
   return s;
+}
+
+// 128-row tiles halve the shared-memory reads per FMA, but double each
+// cluster's partial-tile traffic and halve the CTA count: they are used
+// when they still give over half the SMs a CTA, every CTA at least
+// kMinSlicesPerCta k slices and clusters of at most 4 (measured on B200:
+// 512^3 12.4 us against 13.7 us with 64-row tiles; with clusters of 8 the
+// larger partial tiles cost more than they save); otherwise 64-row tiles.
+SmallPlan planSmall(const kern::GemmParams &p, int sms) {
+  const SmallPlan tall = planFor(p, sms, 128);
+  if (p.m > 64 && tall.ctas() * 2 > sms && tall.per_cta >= kMinSlicesPerCta &&
+      tall.split <= 4)
+    return tall;
+  return planFor(p, sms, 64);
 }
 
 }  // namespace
 
 bool smallEligible(const kern::GemmParams &p, int sms) {
-  const long long tiles_m = ceilDiv(p.m, sm::kBM), tiles_n = ceilDiv(p.n, sm::kBN);
-  if (p.batch > 65535 || tiles_n > 65535 || tiles_m * sm::kMaxSplit * sms > INT_MAX) return false;
+  if (p.batch > 65535 || ceilDiv(p.n, sm::kBN) > 65535 ||
+      ceilDiv(p.m, 64) * sm::kMaxSplit * sms > INT_MAX)
+    return false;
   // The persistent kernel's 128 x 128 tiles would leave most SMs without a
   // whole tile, and each CTA here has little enough work that latency, not
   // FMA throughput, decides the time.
   const long long tiles128 = ceilDiv(p.m, 128) * ceilDiv(p.n, 128) * p.batch;
   if (tiles128 * kSmallTileShare > sms) return false;
   const SmallPlan s = planSmall(p, sms);
-  const double fma_per_cta = static_cast<double>(p.m) * p.n * p.k * p.batch /
-                             (static_cast<double>(s.tiles) * s.split * s.groups);
+  const double fma_per_cta =
+      static_cast<double>(p.m) * p.n * p.k * p.batch / static_cast<double>(s.ctas());
   return fma_per_cta <= kSmallMaxFmaPerCta;
 }
 
@@ -409,7 +476,7 @@ sgblasStatus_t launchSmall(bool ta, bool tb, const kern::GemmParams &gp, const S
   p.ldc = gp.ldc;
   p.alpha = gp.alpha;
   p.beta = gp.beta;
-  const SmallPlan s = planSmall(gp, sms);
+  SmallPlan s = planSmall(gp, sms);
   p.tiles_m = static_cast<int>(s.tiles_m);
   p.slices = s.slices;
   p.split = s.split;
@@ -419,8 +486,9 @@ sgblasStatus_t launchSmall(bool ta, bool tb, const kern::GemmParams &gp, const S
     // [arrival counters | one partial tile per (tile, cluster)], the layout
     // of the tile kernel's stream-K scratch; without it, one cluster per tile.
     const size_t counters = static_cast<size_t>(s.tiles) * s.split;
-    const size_t need = kCounterRegionBytes +
-                        static_cast<size_t>(s.tiles) * p.groups * sm::kGroups * sizeof(float4);
+    const size_t tile_bytes = static_cast<size_t>(s.bm) * sm::kBN * sizeof(float);
+    const size_t need =
+        kCounterRegionBytes + static_cast<size_t>(s.tiles) * p.groups * tile_bytes;
     unsigned char *base = nullptr;
     if (counters * sizeof(int) > kCounterRegionBytes) {
       base = nullptr;
@@ -446,11 +514,9 @@ sgblasStatus_t launchSmall(bool ta, bool tb, const kern::GemmParams &gp, const S
             (gp.batch == 1 || gp.stride_c % 4 == 0);
   const dim3 grid(static_cast<unsigned>(s.tiles_m * p.groups * p.split),
                   static_cast<unsigned>(s.tiles_n), static_cast<unsigned>(gp.batch));
-  sgblasStatus_t st;
-  if (!ta && !tb) st = launchByBeta<false, false>(p, grid, device, stream);
-  else if (!ta && tb) st = launchByBeta<false, true>(p, grid, device, stream);
-  else if (ta && !tb) st = launchByBeta<true, false>(p, grid, device, stream);
-  else st = launchByBeta<true, true>(p, grid, device, stream);
+  const sgblasStatus_t st = s.bm == 128
+                                ? launchByMode<128>(ta, tb, p, grid, device, stream)
+                                : launchByMode<64>(ta, tb, p, grid, device, stream);
   if (st == SGBLAS_STATUS_SUCCESS && used_handle_workspace &&
       !markWorkspaceUse(scratch.ctx, stream))
     return SGBLAS_STATUS_EXECUTION_FAILED;

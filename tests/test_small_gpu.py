@@ -23,10 +23,8 @@ pytestmark = pytest.mark.gpu
 SMS_B200 = 148
 
 
-def _plan(m, n, k, batch=1, sms=SMS_B200):
-    """The launcher's (cluster size, clusters per tile, slices per CTA) on a
-    GPU with `sms` SMs (sgemm_small.cu chooseSplit / chooseGroups)."""
-    tiles = -(-m // 64) * -(-n // 64) * batch
+def _plan_for(m, n, k, batch, sms, bm):
+    tiles = -(-m // bm) * -(-n // 64) * batch
     slices = -(-k // 32)
     split = 1
     while split * 2 <= 8 and split * 2 <= slices and tiles * split * 2 <= sms:
@@ -34,14 +32,24 @@ def _plan(m, n, k, batch=1, sms=SMS_B200):
     groups = 1
     if tiles * split * 2 <= sms:
         groups = max(1, min(sms // (tiles * split), slices // (split * 4)))
-    return split, groups, -(-slices // (split * groups))
+    return split, groups, -(-slices // (split * groups)), bm, tiles * split * groups
+
+
+def _plan(m, n, k, batch=1, sms=SMS_B200):
+    """The launcher's (cluster size, clusters per tile, slices per CTA, tile
+    rows) on a GPU with `sms` SMs (sgemm_small.cu planSmall)."""
+    tall = _plan_for(m, n, k, batch, sms, 128)
+    if m > 64 and tall[4] * 2 > sms and tall[2] >= 4 and tall[0] <= 4:
+        return tall[:4]
+    return _plan_for(m, n, k, batch, sms, 64)[:4]
 
 
 def _split(m, n, k, batch=1):
     return _plan(m, n, k, batch)[0]
 
 
-# (m, n, k): cluster size and clusters per tile in the comment (148 SMs)
+# (m, n, k): cluster size and clusters per tile in the comment (148 SMs);
+# 512^3 and 450 x 300 x 640 run on 128-row tiles
 SHAPES = [(256, 256, 256),    # 8
           (512, 512, 512),    # 2
           (384, 384, 384),    # 4
@@ -53,12 +61,14 @@ SHAPES = [(256, 256, 256),    # 8
           (3, 250, 7),        # 1
           (128, 128, 8192),   # 8 x 4 clusters per tile
           (64, 200, 3000),    # 8 x 2, ragged k and n
-          (37, 19, 4111)]     # 8 x 4, the last cluster's k range is short
+          (37, 19, 4111),     # 8 x 4, the last cluster's k range is short
+          (500, 200, 1000),   # 4
+          (450, 300, 640)]    # 4, 128-row tiles with ragged m and n
 
 
 def _idle_cta(m, n, k):
     """True if some CTA gets no k slice."""
-    split, groups, per_cta = _plan(m, n, k)
+    split, groups, per_cta, _ = _plan(m, n, k)
     return (split * groups - 1) * per_cta >= -(-k // 32)
 
 
@@ -66,6 +76,7 @@ def test_shape_list_covers_every_cluster_size():
     plans = [_plan(*s) for s in SHAPES]
     assert {p[0] for p in plans} == {1, 2, 4, 8}
     assert {p[1] for p in plans} >= {1, 2, 4}
+    assert {p[3] for p in plans} == {64, 128}
     assert any(_idle_cta(*s) for s in SHAPES)
 
 
