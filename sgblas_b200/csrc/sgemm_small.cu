@@ -1,24 +1,28 @@
 // The small-problem kernel: products too small to fill the GPU with the
-// persistent tile kernel's 128-row tiles (256^3, 512^3, a few small batched
-// matrices).
+// persistent tile kernel's 128 x 128 tiles (256^3, 512^3, deep-k products
+// with a small C, a few small batched matrices).
 //
 // Replaces the reference's small kernel family (64-row tiles,
 // src/sgemm_cuda.cu:598-640, sgemm_async_sm80_small.hpp) with a design for
 // 148 SMs:
-//   - C is cut into 64 x 64 tiles. Each tile belongs to one thread-block
-//     cluster of `split` CTAs (1, 2, 4 or 8) that divide its k range; split
-//     is the largest that keeps tiles x split within one CTA per SM, so a
-//     256^3 product runs on 128 SMs instead of 16.
+//   - C is cut into 64- or 128-row x 64-column tiles. Each tile's k range is
+//     divided among `groups` thread-block clusters of `split` CTAs (split 1,
+//     2, 4 or 8; groups > 1 only for deep k), chosen to give as many SMs as
+//     possible one CTA: a 256^3 product runs on 128 SMs instead of 16.
 //   - Every CTA stages its k slices (32 deep) with 4-byte cp.async into a
 //     4-stage ring, any alignment, leading dimension or transpose, with zero
-//     fill outside the matrix; 256 threads each compute a 4 x 4 block of the
-//     tile with paired FMAs (fma.rn.f32x2), as the large kernel does.
+//     fill outside the matrix; 256 threads each compute a 4 x 4 (or 8 x 4)
+//     block of the tile with paired FMAs (fma.rn.f32x2), reading the next
+//     k step's fragments while the current one computes.
 //   - The cluster's partial tiles are summed through distributed shared
 //     memory: CTA r reads its 1/split share of the tile from every CTA of the
-//     cluster in rank order (so results are deterministic), applies the
-//     alpha/beta epilogue and writes C. No workspace, counters or atomics:
+//     cluster in rank order. With one cluster per tile it then applies the
+//     alpha/beta epilogue and writes C: no workspace, counters or atomics, so
 //     the kernel runs the same way from sgblasSgemm, sgblasSgemmNoAlloc and
-//     inside a CUDA graph.
+//     inside a CUDA graph. With several clusters per tile, each stores its
+//     sum in the stream-K scratch and the last cluster to arrive (an arrival
+//     counter per tile and share) adds the stored sums in cluster order.
+//     Either way the summation order is fixed: results are deterministic.
 //   - Programmatic dependent launch: the prologue overlaps the previous
 //     kernel on the stream, and global memory is first read after
 //     griddepcontrol.wait.
@@ -271,7 +275,9 @@ __global__ void __launch_bounds__(kThreads, 1) smallKernel(const __grid_constant
       }
     }
   }
-  clusterSync();   // the other CTAs have read this CTA's partial tile
+  // The other CTAs have read this CTA's partial tile (every read's value has
+  // been added into sum[] before its CTA arrives).
+  clusterSyncRelaxed();
 
   if (groups > 1) {
     // Several clusters share the tile: each stores its sum, and for every
