@@ -177,12 +177,15 @@ __global__ void __launch_bounds__(kThreads, 1) smallKernel(const __grid_constant
     cpAsyncCommit();
     const float *as = smem + (i % kStages) * kStageFloats + ty * kTM;
     const float *bs = smem + (i % kStages) * kStageFloats + kTileA + tx * kTN;
-    // Fragments of step kk + 1 are read while step kk computes.
+    // Fragments of step kk + 1 are read while step kk computes. The 64-row
+    // loop is unrolled 4 steps deep, not 32: a small product runs this code
+    // once per SM from a cold instruction cache, and the shorter loop took
+    // 256^3 from 8.3 to 6.2 us per call (back to back, B200).
     float4 a[kTM / 4], b;
 #pragma unroll
     for (int v = 0; v < kTM / 4; ++v) a[v] = *reinterpret_cast<const float4 *>(as + 4 * v);
     b = *reinterpret_cast<const float4 *>(bs);
-#pragma unroll
+#pragma unroll (kBM == 64 ? 4 : kBK)
     for (int kk = 0; kk < kBK; ++kk) {
       float4 an[kTM / 4], bn = b;
 #pragma unroll
