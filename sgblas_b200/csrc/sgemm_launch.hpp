@@ -123,10 +123,10 @@ sgblasStatus_t launchTf32(bool ta, bool tb, const kern::GemmParams &p, const Scr
 // partial tiles through distributed shared memory (and, with several
 // clusters per tile, through the stream-K scratch); any alignment, leading
 // dimension, transpose or batch form. Chosen when the persistent kernel's
-// 128 x 128 tiles number at most SMs / kSmallTileShare and each CTA of the
-// cluster kernel has at most kSmallMaxFmaPerCta multiply-adds.
+// 128 x 128 tiles number at most SMs / kSmallTileShare and the busiest SM
+// of the cluster kernel has at most kSmallMaxFmaPerSm multiply-adds.
 constexpr long long kSmallTileShare = 4;
-constexpr double kSmallMaxFmaPerCta = 2097152.0;   // 2^21 (512^3: 2^20 on 148 SMs)
+constexpr double kSmallMaxFmaPerSm = 2097152.0;   // 2^21 (512^3: 2^20 on 148 SMs)
 bool smallEligible(const kern::GemmParams &p, int sms);
 // p carries pointers, sizes, scalars and the batch (strides or arrays).
 sgblasStatus_t launchSmall(bool ta, bool tb, const kern::GemmParams &p, const Scratch &scratch,

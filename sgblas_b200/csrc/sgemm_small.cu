@@ -130,7 +130,8 @@ __device__ __forceinline__ float4 loadC(const float *cp, int rows, bool vec) {
 }
 
 template <int kBM, bool kTA, bool kTB, Beta kBeta>
-__global__ void __launch_bounds__(kThreads, 1) smallKernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, kBM == 64 ? 2 : 1)
+    smallKernel(const __grid_constant__ Params p) {
   using T = Tile<kBM>;
   constexpr int kTM = T::kTM, kRowA = T::kRowA, kTileA = T::kTileA;
   constexpr int kStageFloats = T::kStageFloats, kColGroups = T::kColGroups;
@@ -393,26 +394,31 @@ sgblasStatus_t launchByMode(bool ta, bool tb, const sm::Params &p, dim3 grid, in
   return launchByBeta<kBM, true, true>(p, grid, device, stream);
 }
 
-// CTAs per cluster: the largest power of two up to kMaxSplit that keeps one
-// CTA per SM and at least one k slice per CTA.
-int chooseSplit(long long tiles, int slices, int sms) {
+// CTAs per cluster: the largest power of two up to kMaxSplit that keeps the
+// CTAs within `slots` (resident CTAs the GPU holds at once) and at least one
+// k slice per CTA.
+int chooseSplit(long long tiles, int slices, long long slots) {
   int split = 1;
-  while (split * 2 <= sm::kMaxSplit && split * 2 <= slices && tiles * split * 2 <= sms)
+  while (split * 2 <= sm::kMaxSplit && split * 2 <= slices && tiles * split * 2 <= slots)
     split *= 2;
   return split;
 }
 
 // Clusters per tile: more than one only when the tiles' clusters would
-// leave over half the SMs idle and k is deep enough to give every CTA
+// leave over half the slots empty and k is deep enough to give every CTA
 // kMinSlicesPerCta slices.
 constexpr int kMinSlicesPerCta = 4;
-int chooseGroups(long long tiles, int split, int slices, int sms) {
+int chooseGroups(long long tiles, int split, int slices, long long slots) {
   const long long ctas = tiles * split;
-  if (ctas * 2 > sms) return 1;
-  const long long by_sms = sms / ctas;
+  if (ctas * 2 > slots) return 1;
+  const long long by_slots = slots / ctas;
   const long long by_k = slices / (static_cast<long long>(split) * kMinSlicesPerCta);
-  return static_cast<int>(std::max(1LL, std::min(by_sms, by_k)));
+  return static_cast<int>(std::max(1LL, std::min(by_slots, by_k)));
 }
+
+// Resident CTAs per SM: two of the 64-row kernel (at most 128 registers per
+// thread and 70 KB of shared memory each), one of the 128-row kernel.
+constexpr int ctasPerSm(int bm) { return bm == 64 ? 2 : 1; }
 
 struct SmallPlan {
   int bm;   // tile rows: 64 or 128
@@ -428,8 +434,13 @@ SmallPlan planFor(const kern::GemmParams &p, int sms, int bm) {
   s.tiles_n = ceilDiv(p.n, sm::kBN);
   s.tiles = s.tiles_m * s.tiles_n * p.batch;
   s.slices = static_cast<int>(ceilDiv(p.k, sm::kBK));
+  // Clusters are sized for one CTA per SM; extra clusters for deep k may
+  // fill every slot (measured on B200: two CTAs per SM took 128 x 128 x 8192
+  // from 25.1 to 19.3 us, but slowed 384^3 from 10.7 to 12.8 us when used
+  // for larger clusters).
   s.split = chooseSplit(s.tiles, s.slices, sms);
-  s.groups = chooseGroups(s.tiles, s.split, s.slices, sms);
+  s.groups = chooseGroups(s.tiles, s.split, s.slices,
+                          static_cast<long long>(sms) * ctasPerSm(bm));
   s.per_cta = static_cast<int>(ceilDiv(s.slices, static_cast<long long>(s.split) * s.groups));
   return s;
 }
@@ -460,9 +471,11 @@ bool smallEligible(const kern::GemmParams &p, int sms) {
   const long long tiles128 = ceilDiv(p.m, 128) * ceilDiv(p.n, 128) * p.batch;
   if (tiles128 * kSmallTileShare > sms) return false;
   const SmallPlan s = planSmall(p, sms);
-  const double fma_per_cta =
-      static_cast<double>(p.m) * p.n * p.k * p.batch / static_cast<double>(s.ctas());
-  return fma_per_cta <= kSmallMaxFmaPerCta;
+  // Multiply-adds on the busiest SM (CTAs are spread over the SMs first).
+  const long long ctas = s.ctas();
+  const double fma_per_sm = static_cast<double>(p.m) * p.n * p.k * p.batch /
+                            static_cast<double>(ctas) * static_cast<double>(ceilDiv(ctas, sms));
+  return fma_per_sm <= kSmallMaxFmaPerSm;
 }
 
 sgblasStatus_t launchSmall(bool ta, bool tb, const kern::GemmParams &gp, const Scratch &scratch,

@@ -29,9 +29,10 @@ def _plan_for(m, n, k, batch, sms, bm):
     split = 1
     while split * 2 <= 8 and split * 2 <= slices and tiles * split * 2 <= sms:
         split *= 2
+    slots = sms * (2 if bm == 64 else 1)   # resident CTAs: two 64-row CTAs per SM
     groups = 1
-    if tiles * split * 2 <= sms:
-        groups = max(1, min(sms // (tiles * split), slices // (split * 4)))
+    if tiles * split * 2 <= slots:
+        groups = max(1, min(slots // (tiles * split), slices // (split * 4)))
     return split, groups, -(-slices // (split * groups)), bm, tiles * split * groups
 
 
@@ -59,7 +60,7 @@ SHAPES = [(256, 256, 256),    # 8
           (65, 129, 33),      # 2 (two slices)
           (1, 1, 1),          # 1
           (3, 250, 7),        # 1
-          (128, 128, 8192),   # 8 x 4 clusters per tile
+          (128, 128, 8192),   # 8 x 8 clusters per tile (two CTAs per SM)
           (64, 200, 3000),    # 8 x 2, ragged k and n
           (37, 19, 4111),     # 8 x 4, the last cluster's k range is short
           (500, 200, 1000),   # 4
