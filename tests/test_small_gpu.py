@@ -54,7 +54,8 @@ def _split(m, n, k, batch=1):
 SHAPES = [(256, 256, 256),    # 8
           (512, 512, 512),    # 2
           (384, 384, 384),    # 4
-          (700, 600, 50),     # 1 (110 tiles)
+          (700, 600, 50),     # 1 (110 tiles): launched without clusters
+          (700, 600, 256),    # 2, 128-row tiles
           (64, 64, 150),      # 4: five slices, the last CTA has none
           (100, 37, 1000),    # 8, ragged tiles
           (65, 129, 33),      # 2 (two slices)
