@@ -8,7 +8,9 @@
 //   - C is cut into 64- or 128-row x 64-column tiles. Each tile's k range is
 //     divided among `groups` thread-block clusters of `split` CTAs (split 1,
 //     2, 4 or 8; groups > 1 only for deep k), chosen to give as many SMs as
-//     possible one CTA: a 256^3 product runs on 128 SMs instead of 16.
+//     possible one CTA: a 256^3 product runs on 128 SMs instead of 16. The
+//     extra clusters of a deep-k product may put two 64-row CTAs on an SM.
+//     Without a split (split 1) the kernel is launched without clusters.
 //   - Every CTA stages its k slices (32 deep) with 4-byte cp.async into a
 //     4-stage ring, any alignment, leading dimension or transpose, with zero
 //     fill outside the matrix; 256 threads each compute a 4 x 4 (or 8 x 4)
