@@ -223,6 +223,32 @@ def test_tf32_pair_cta_stream_k(cuda, tf32_handle, ta, tb):
 
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_tf32_small_deep_k_pieces(cuda, tf32_handle, ta, tb):
+    """640 x 520 x 4100: 25 single-CTA tiles of 128 x 128 with 129 k slices,
+    each tile split into pieces of at least 1024 k that meet in the
+    workspace (ragged last tile row and column, k tail); integer inputs make
+    the result exact, then a random case is checked against the TF32 bound."""
+    torch = cuda
+    m, n, k = 640, 520, 4100
+    lda, ldb = (k if ta else m), (n if tb else k)
+    rng = np.random.default_rng(80 + 2 * ta + tb)
+    a = rng.integers(-2, 3, lda * (m if ta else k)).astype(np.float32)
+    b = rng.integers(-2, 3, ldb * (k if tb else n)).astype(np.float32)
+    case = C.Case("tf32-deep", ta, tb, m, n, k, lda, ldb, m, 1.0, 0.0)
+    c = np.full(m * n, np.nan, np.float32)
+    status, out = run_sgemm(torch, tf32_handle, case, a, b, c)
+    assert status == 0
+    ref, _ = oracle.sgemm_f64(ta, tb, m, n, k, 1.0, a, lda, b, ldb, 0.0, c, m)
+    assert np.array_equal(c_view(out, m, n, m).astype(np.float64), ref)
+    case = C.Case("tf32-deep-rand", ta, tb, m, n, k, lda, ldb, m + 2, 0.75, -0.5)
+    a, b, c = C.cfg_inputs(case, 81, None)
+    status, out = run_sgemm(torch, tf32_handle, case, a, b, c)
+    assert status == 0
+    check_tf32(case, a, b, c, out, (ta, tb))
+    assert sg.get_device_errors() == 0
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("m,n,k,count", [(300, 200, 70, 3), (1024, 1024, 96, 5)])
 def test_tf32_strided_batched(cuda, tf32_handle, ta, tb, m, n, k, count):
     """Strided batches on the tensor cores (3-D tensor maps, batch-major
