@@ -237,13 +237,6 @@ __device__ __forceinline__ void clusterSync() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// Whole-cluster barrier without memory ordering: for "every CTA has finished
-// reading my shared memory", where each CTA's reads have already completed
-// (their values were consumed) before it arrives.
-__device__ __forceinline__ void clusterSyncRelaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
-}
 // Arrive on an mbarrier in any CTA of the cluster (cluster address).
 __device__ __forceinline__ void mbarArriveCluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)

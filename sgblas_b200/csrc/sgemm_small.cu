@@ -289,9 +289,11 @@ __global__ void __launch_bounds__(kThreads, kBM == 64 ? 2 : 1)
       }
     }
   }
-  // The other CTAs have read this CTA's partial tile (every read's value has
-  // been added into sum[] before its CTA arrives).
-  if (split > 1) clusterSyncRelaxed();
+  // The other CTAs have read this CTA's partial tile before it may exit. The
+  // arrive has release semantics so that each CTA's distributed-shared-memory
+  // reads are complete before it counts as arrived, whatever order the
+  // compiler gives the adds that consume them.
+  if (split > 1) clusterSync();
 
   if (groups > 1) {
     // Several clusters share the tile: each stores its sum, and for every
