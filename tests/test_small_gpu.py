@@ -204,6 +204,37 @@ def test_small_graph_capture_on_fresh_handle(cuda, m, n, k):
     assert sg.get_device_errors() == 0
 
 
+def test_shared_workspace_counters_alternate(cuda, handle):
+    """One handle alternating between deep-k cluster launches (arrival
+    counters and partial tiles in the handle's workspace) and stream-K tile
+    kernel launches (counters and slots at the same offsets), without a host
+    sync in between: every launch must leave its counters at zero for the
+    next, so each result equals the one a fresh handle computes."""
+    torch = cuda
+    cases = [C.Case("alt-small", 0, 0, 128, 128, 8192, 128, 8192, 128, 1.0, 0.0),
+             C.Case("alt-tile", 0, 1, 1500, 1300, 3000, 1500, 1300, 1500, 0.5, 1.0),
+             C.Case("alt-small2", 1, 0, 64, 200, 3000, 3000, 3000, 64, -1.0, 0.5)]
+    inputs, expect = [], []
+    for i, case in enumerate(cases):
+        a, b, c = C.cfg_inputs(case, 950 + i, None)
+        with sg.Handle() as fresh:
+            _, out = run_sgemm(torch, fresh, case, a, b, c)
+        inputs.append((to_device(torch, a), to_device(torch, b), c))
+        expect.append(out)
+    outs = []
+    torch.cuda.synchronize()
+    for rep in range(3):
+        for case, ((_, pa), (_, pb), c) in zip(cases, inputs):
+            dc, pc = to_device(torch, c)
+            handle.sgemm(case.transa, case.transb, case.m, case.n, case.k, case.alpha, pa,
+                         case.lda, pb, case.ldb, case.beta, pc, case.ldc)
+            outs.append(dc)
+    torch.cuda.synchronize()
+    for i, dc in enumerate(outs):
+        assert np.array_equal(dc.cpu().numpy(), expect[i % len(cases)]), (i, cases[i % 3].name)
+    assert sg.get_device_errors() == 0
+
+
 def test_kernel_selection(cuda, handle):
     """Small products launch the cluster kernel, larger ones the persistent
     tile kernel (kernel names from the profiler's CUDA activity)."""
