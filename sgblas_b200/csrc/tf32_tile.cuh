@@ -5,8 +5,8 @@
 // is outside the strict-FP32 contract of the default math mode and is only
 // used when the caller selects SGBLAS_MATH_TF32.
 //
-// One persistent CTA per SM walks 128 x N tiles of C (N = 256, or 128 when
-// that fills the last wave better). Warp roles:
+// One persistent CTA per SM walks 128 x N tiles of C (N = 256, or 128 or 64
+// when that fills the GPU better). Warp roles:
 //   warp 0   TMA producer: 128x32 A and Nx32 B tiles into a stage ring,
 //            128-byte swizzled (16-byte atoms for K-major tiles, 32-byte
 //            atoms for MN-major ones: the canonical UMMA layouts);
@@ -49,18 +49,19 @@ constexpr int kEpilogueWarp0 = 4;
 // per round trip to L2 in each pass).
 constexpr int kGatherChunks = 2;
 
-// Tile width N (UMMA N): 256, or 128 where the 256-wide tiles would leave a
-// poorly filled last wave. The stage ring fills about 192 KiB either way.
+// Tile width N (UMMA N): 256, 128 where the 256-wide tiles would leave a
+// poorly filled last wave, or 64 where even 128-wide tiles would leave over
+// half the SMs without one. The stage ring fills about 192 KiB each way.
 template <int kBN_>
 struct Cfg {
   static constexpr int kBN = kBN_;
   static constexpr int kBBytes = kBN * kBK * 4;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = kBN == 256 ? 4 : 6;
+  static constexpr int kStages = kBN == 256 ? 4 : kBN == 128 ? 6 : 8;
   static constexpr int kTmemColumns = kAccums * kBN;   // 512 or 256
   static constexpr int kBarrierBytes = 8 * (2 * kStages + 2 * kAccums);
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
-  static_assert(kBN == 128 || kBN == 256, "tile width");
+  static_assert(kBN == 64 || kBN == 128 || kBN == 256, "tile width");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 };
 

@@ -51,7 +51,11 @@ def tf32_handle(handle):
     handle.set_math_mode(sg.SGBLAS_MATH_FP32)
 
 
-SHAPES = [(300, 200, 70), (257, 513, 100), (128, 256, 32), (1, 1, 1), (640, 768, 999)]
+# 64-wide tiles for the first three and the last but one (128-wide tiles
+# would leave over half the SMs idle), 128-wide for (1, 1, 1) and
+# 1152 x 1200 (90 tiles of 128 x 128 for 148 SMs).
+SHAPES = [(300, 200, 70), (257, 513, 100), (128, 256, 32), (1, 1, 1), (640, 768, 999),
+          (1152, 1200, 200)]
 
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
