@@ -48,12 +48,14 @@ int isSm100(int device);
 // Persistent schedule: one CTA per SM. Whole tiles are dealt round-robin;
 // when the tile count leaves a partial last wave, the last (full wave +
 // remainder) tiles are split by k iterations over all CTAs (stream-K), so every
-// SM finishes at the same time. Small problems with fewer tiles than SMs are
-// split the same way, down to kMinSkIters k slices per CTA.
+// SM finishes at the same time. Problems with fewer tiles than SMs are split
+// the same way, down to kMinSkIters k slices per CTA, or into the same whole
+// number of pieces per tile when that costs less (see makeSchedule).
 struct Schedule {
   int grid = 0, dp_tiles = 0, sk_tiles = 0, sk_q = 0, sk_r = 0;
 };
 constexpr int kMinSkIters = 4;
+constexpr int kItemCostIters = 3;   // a stream-K part's fix-up and epilogue, in k iterations
 Schedule makeSchedule(long long tiles, int kiters, int sms);
 
 // Scratch layout: [arrival counters (kCounterRegionBytes) | partial slots].
