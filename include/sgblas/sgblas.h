@@ -63,9 +63,13 @@ sgblasStatus_t sgblasDestroy(sgblasHandle_t handle);
 sgblasStatus_t sgblasSetStream(sgblasHandle_t handle, sgblasStream_t stream);
 sgblasStatus_t sgblasGetStream(sgblasHandle_t handle, sgblasStream_t *stream);
 
-/* FP32 (default) or TF32. TF32 is accepted and stored, but any call that
- * would do work in TF32 mode returns NOT_SUPPORTED: this library only
- * computes strict FP32 (FP32 multiply, FP32 accumulate, no tensor cores). */
+/* FP32 (default) or TF32. FP32 computes strict FP32 on CUDA cores (FP32
+ * multiply, FP32 accumulate, no tensor cores). TF32 selects the tensor-core
+ * lane: operands rounded to TF32 (10-bit mantissa), FP32 accumulation, error
+ * within (2^-9 + (k+2) * 2^-22) * (|alpha| sum|a*b| + |beta*c|) per element;
+ * operands the tensor-core lane cannot read in place (and pointer-array
+ * batches) are computed in strict FP32 instead. The reference returns
+ * NOT_SUPPORTED for work in TF32 mode. */
 sgblasStatus_t sgblasSetMathMode(sgblasHandle_t handle, sgblasMathMode_t mode);
 sgblasStatus_t sgblasGetMathMode(sgblasHandle_t handle, sgblasMathMode_t *mode);
 

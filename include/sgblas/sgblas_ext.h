@@ -24,6 +24,16 @@ sgblasStatus_t sgblasGetDeviceErrors(unsigned *flags, int clear);
  * usable. Synchronizes the current device. No counterpart in the reference. */
 sgblasStatus_t sgblasSelfTestWaitTimeout(unsigned polls, int *timed_out);
 
+/* Test hook for split-tile recovery. Leaves the handle workspace's arrival
+ * counters in the state a split launch that stopped early (a bounded wait
+ * that timed out) leaves behind -- every counter holding one arrival of the
+ * handle's latest launch -- so that a test can check that the next split
+ * product on the handle is still exact. Enqueued on the handle's stream, on
+ * the current device, which must be the workspace's. Returns
+ * SGBLAS_STATUS_NOT_SUPPORTED while the handle has no workspace.
+ * No counterpart in the reference (it splits no tile across CTAs). */
+sgblasStatus_t sgblasTestInterruptScratch(sgblasHandle_t handle);
+
 /* sgblasSgemm for callers that cannot allocate device memory (their process
  * or host owns the allocator, or forbids allocation after start-up). Same
  * arguments, semantics and status codes as sgblasSgemm, but instead of the

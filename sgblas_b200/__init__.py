@@ -58,6 +58,7 @@ _SIGNATURES = {
     "sgblasGetStatusString": (ctypes.c_char_p, [ctypes.c_int]),
     "sgblasGetDeviceErrors": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]),
     "sgblasSelfTestWaitTimeout": (ctypes.c_int, [ctypes.c_uint, ctypes.POINTER(ctypes.c_int)]),
+    "sgblasTestInterruptScratch": (ctypes.c_int, [ctypes.c_void_p]),
     "sgblasSgemmStridedBatched": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                                  ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                  _c_float_p, ctypes.c_void_p, ctypes.c_int,

@@ -71,11 +71,15 @@ def build(verbose: bool = False) -> pathlib.Path:
     srcs = _sources()
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
-    if LIB.exists() and LIB.stat().st_mtime >= max(o.stat().st_mtime for o in objs):
+    link_deps = [o.stat().st_mtime for o in objs] + [(CSRC / "exports.map").stat().st_mtime,
+                                                      pathlib.Path(__file__).stat().st_mtime]
+    if LIB.exists() and LIB.stat().st_mtime >= max(link_deps):
         return LIB
     tmp = LIB.with_suffix(".so.tmp")
+    # Only the C API is exported (csrc/exports.map).
     cmd = [_nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(tmp),
-           *map(str, objs), "-ldl", "-lpthread", "-lrt"]
+           *map(str, objs), "-ldl", "-lpthread", "-lrt",
+           "-Xlinker", f"--version-script={CSRC / 'exports.map'}"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"linking libsgblas.so failed:\n{res.stdout}\n{res.stderr}")

@@ -24,6 +24,9 @@ struct sgblasContext {
   std::size_t workspace_bytes = 0;
   int workspace_device = -1;
   void *workspace_event = nullptr;
+  // Epoch of the last launch that used the workspace's arrival counters
+  // (each such launch takes the next one; see kern::arriveCounter).
+  unsigned workspace_epoch = 0;
 };
 
 namespace sgblas::detail {

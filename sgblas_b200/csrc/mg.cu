@@ -159,7 +159,6 @@ extern "C" sgblasStatus_t sgblasMgSgemm(sgblasMgHandle_t handle, sgblasOperation
   const bool product = m > 0 && k > 0 && alpha != nullptr && *alpha != 0.0F;
   if (product) {
     if (a == nullptr) return SGBLAS_STATUS_INVALID_VALUE;
-    if (handle->inner->math_mode != SGBLAS_MATH_FP32) return SGBLAS_STATUS_NOT_SUPPORTED;
     const NcclApi *api = nccl();
     if (api == nullptr) return SGBLAS_STATUS_NOT_SUPPORTED;
     const size_t count = static_cast<size_t>(lda) *

@@ -20,6 +20,37 @@ constexpr uint32_t kSpinLimit = 1u << 24;
 
 // Device error word codes (OR-ed together).
 constexpr unsigned kErrBarrierTimeout = 1u;
+constexpr unsigned kErrCounter = 2u;   // an arrival counter could not be updated
+
+// ---- split-tile arrival counters --------------------------------------------
+// A tile split into pieces is finished by the CTA whose piece arrives last.
+// Its counter holds (epoch << 32) | arrivals. The host gives every launch
+// that uses a scratch buffer's counters an epoch that no earlier launch on
+// that buffer used, so a counter holding any other epoch -- zero, or what a
+// launch that stopped early (a wait that timed out) left behind -- reads as
+// no arrivals: an interrupted launch cannot make a later one pick the wrong
+// last piece. The last arrival resets its counter to zero, so a CUDA graph
+// that replays one epoch also starts from clean counters.
+constexpr int kCounterCasLimit = 1 << 16;   // far above any tile's piece count
+
+// Counts one arrival of launch `epoch` (non-zero) and returns its number (1
+// for the first piece), or 0 after raising kErrCounter if the update kept
+// failing. Each failed compare-and-swap means another piece arrived, so
+// kCounterCasLimit is never reached in a valid launch.
+__device__ __forceinline__ unsigned arriveCounter(unsigned long long *counter, unsigned epoch,
+                                                  unsigned *err) {
+  unsigned long long seen = 0;
+  for (int i = 0; i < kCounterCasLimit; ++i) {
+    const unsigned long long want = static_cast<unsigned>(seen >> 32) == epoch
+                                        ? seen + 1
+                                        : (static_cast<unsigned long long>(epoch) << 32) | 1ULL;
+    const unsigned long long got = atomicCAS(counter, seen, want);
+    if (got == seen) return static_cast<unsigned>(want & 0xffffffffULL);
+    seen = got;
+  }
+  if (err != nullptr) atomicOr(err, kErrCounter);
+  return 0;
+}
 
 __device__ __forceinline__ uint32_t smemAddr(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -273,7 +273,7 @@ bool ensureWorkspace(sgblasContext *ctx, size_t need, int device, cudaStream_t s
     (void)cudaGetLastError();
     return false;
   }
-  // Counters must start at zero; every launch leaves them at zero again.
+  // Counters start at zero: epoch 0, which no launch uses.
   if (cudaMemsetAsync(ws, 0, std::min(bytes, kCounterRegionBytes), stream) != cudaSuccess ||
       cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
     (void)cudaGetLastError();
@@ -284,6 +284,27 @@ bool ensureWorkspace(sgblasContext *ctx, size_t need, int device, cudaStream_t s
   ctx->workspace_bytes = bytes;
   ctx->workspace_device = device;
   ctx->workspace_event = ev;
+  return true;
+}
+
+unsigned nextCounterEpoch(sgblasContext *ctx, cudaStream_t stream) {
+  unsigned epoch = ctx->workspace_epoch + 1;
+  if (epoch == 0) {
+    if (cudaMemsetAsync(ctx->workspace, 0, kCounterRegionBytes, stream) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return 0;
+    }
+    epoch = 1;
+  }
+  ctx->workspace_epoch = epoch;
+  return epoch;
+}
+
+bool clearFixedCounters(unsigned char *fixed, size_t count, cudaStream_t stream) {
+  if (cudaMemsetAsync(fixed, 0, count * sizeof(Counter), stream) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
   return true;
 }
 
@@ -461,6 +482,35 @@ extern "C" sgblasStatus_t sgblasSgemm(sgblasHandle_t handle, sgblasOperation_t t
   if (plan.work == Work::kScale) return launchScale(m, n, plan.beta, c, ldc, one, stream);
   return launchProduct(handle, transa, transb, m, n, k, plan.alpha, a, lda, b, ldb, plan.beta, c,
                        ldc, one, stream);
+}
+
+// Test hook: the counter state a split launch that stopped early leaves
+// behind (one arrival of the handle's latest epoch on every counter).
+namespace sgblas::detail {
+namespace {
+__global__ void interruptedCountersKernel(Counter *counters, int count, Counter value) {
+  for (int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x); i < count;
+       i += static_cast<int>(gridDim.x * blockDim.x))
+    counters[i] = value;
+}
+}  // namespace
+}  // namespace sgblas::detail
+
+extern "C" sgblasStatus_t sgblasTestInterruptScratch(sgblasHandle_t handle) {
+  using namespace sgblas::detail;
+  if (handle == nullptr) return SGBLAS_STATUS_NOT_INITIALIZED;
+  if (handle->workspace == nullptr) return SGBLAS_STATUS_NOT_SUPPORTED;
+  int current = -1;
+  if (cudaGetDevice(&current) != cudaSuccess || current != handle->workspace_device) {
+    (void)cudaGetLastError();
+    return SGBLAS_STATUS_INVALID_VALUE;
+  }
+  const auto stream = static_cast<cudaStream_t>(handle->stream);
+  const Counter value = (static_cast<Counter>(handle->workspace_epoch) << 32) | 1ULL;
+  constexpr int kCount = static_cast<int>(kCounterRegionBytes / sizeof(Counter));
+  interruptedCountersKernel<<<4, 256, 0, stream>>>(static_cast<Counter *>(handle->workspace),
+                                                   kCount, value);
+  return launchStatus(cudaGetLastError());
 }
 
 // Batched forms (no counterpart in the reference, whose v1 design lists

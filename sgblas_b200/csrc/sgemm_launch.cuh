@@ -36,22 +36,25 @@ sgblasStatus_t launchTiles(kern::GemmParams p, const Scratch &scratch, int devic
   bool used_handle_workspace = false;
   if (s.sk_tiles > 0) {
     const size_t need = kCounterRegionBytes + 2 * static_cast<size_t>(s.grid) * G::kSlotBytes;
-    const bool counters_fit = static_cast<size_t>(s.sk_tiles) * sizeof(int) <= kCounterRegionBytes;
+    const bool counters_fit =
+        static_cast<size_t>(s.sk_tiles) * sizeof(Counter) <= kCounterRegionBytes;
     unsigned char *base = nullptr;
     if (scratch.fixed != nullptr) {
       // Fixed scratch: refuse rather than allocate. The counters are cleared
       // in case an earlier launch did not finish.
       if (!counters_fit || need > scratch.fixed_bytes) return SGBLAS_STATUS_NOT_SUPPORTED;
-      if (cudaMemsetAsync(scratch.fixed, 0, static_cast<size_t>(s.sk_tiles) * sizeof(int),
-                          stream) != cudaSuccess)
-        return launchStatus(cudaErrorUnknown);
+      if (!clearFixedCounters(scratch.fixed, static_cast<size_t>(s.sk_tiles), stream))
+        return SGBLAS_STATUS_EXECUTION_FAILED;
       base = scratch.fixed;
+      p.epoch = 1;
     } else if (counters_fit && ensureWorkspace(scratch.ctx, need, device, stream)) {
+      p.epoch = nextCounterEpoch(scratch.ctx, stream);
+      if (p.epoch == 0) return SGBLAS_STATUS_EXECUTION_FAILED;
       base = static_cast<unsigned char *>(scratch.ctx->workspace);
       used_handle_workspace = true;
     }
     if (base != nullptr) {
-      p.counters = reinterpret_cast<int *>(base);
+      p.counters = reinterpret_cast<Counter *>(base);
       p.ws = reinterpret_cast<float4 *>(base + kCounterRegionBytes);
     } else {  // no workspace: whole tiles only
       s = Schedule{};

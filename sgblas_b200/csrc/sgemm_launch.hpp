@@ -59,12 +59,14 @@ constexpr int kItemCostIters = 3;   // a stream-K part's fix-up and epilogue, in
 Schedule makeSchedule(long long tiles, int kiters, int sms);
 
 // Scratch layout: [arrival counters (kCounterRegionBytes) | partial slots].
-// sk_tiles <= 2 * grid <= 2 * SMs, so 1024 counters cover any GPU with up to
-// 512 SMs; the counter region has a fixed size so that the layout is the same
-// for every call (counters left at zero by one launch must never be
-// overlapped by another launch's slots).
+// Counters are 8 bytes (epoch and arrivals, kern::arriveCounter); sk_tiles <=
+// 2 * grid <= 2 * SMs, so 1024 counters cover any GPU with up to 512 SMs. The
+// counter region has a fixed size so that the layout is the same for every
+// call (one launch's counters must never be overlapped by another launch's
+// slots).
 constexpr size_t kSlotBytes = kern::Geo<16>::kSlotBytes;  // the largest slot (128 KiB)
-constexpr size_t kCounterRegionBytes = 4096;
+constexpr size_t kCounterRegionBytes = 8192;
+using Counter = unsigned long long;
 
 // A batch of products sharing sizes, leading dimensions and scalars: matrix
 // i is A + i*stride_a (B, C alike), or a_ptrs[i] etc. when the caller passed
@@ -107,6 +109,14 @@ sgblasStatus_t launchPack(const float *src, int ld, bool k_contiguous, int rows_
 bool ensureWorkspace(sgblasContext *ctx, size_t bytes, int device, cudaStream_t stream);
 // Marks the end of a launch that used the handle workspace.
 bool markWorkspaceUse(sgblasContext *ctx, cudaStream_t stream);
+// Counter epoch for the next launch that uses the handle workspace's arrival
+// counters: one more than the last (never 0). When the 32-bit epoch wraps,
+// every counter is first cleared on `stream`, so that no value an earlier
+// launch left can match. 0 if that clear could not be enqueued.
+unsigned nextCounterEpoch(sgblasContext *ctx, cudaStream_t stream);
+// Clears `count` counters of a fixed scratch array on `stream` (launches on
+// a fixed array use epoch 1 after the clear). False if it cannot be enqueued.
+bool clearFixedCounters(unsigned char *fixed, size_t count, cudaStream_t stream);
 
 // The TF32 lane (tf32.cu): the tensor-core kernel reads both operands with
 // TMA, so their bases must be 16-byte aligned and their leading dimensions

@@ -83,7 +83,9 @@ struct Params {
   int per_cta;    // slices per CTA: CTA r of cluster g owns chunk g*split + r
   int c_vec;      // C columns can be read and written as float4
   float4 *ws;     // groups > 1: one partial tile per (tile, cluster)
-  int *counters;  // groups > 1: arrivals per (tile, rank), zero between launches
+  unsigned long long *counters;  // groups > 1: arrivals per (tile, rank) (arriveCounter)
+  unsigned epoch;                // this launch's counter epoch
+  unsigned *err;                 // device error word
 };
 
 // Issues the copies of one operand's kX x kBK slice into a [k][x] buffer
@@ -309,8 +311,9 @@ __global__ void __launch_bounds__(kThreads, kBM == 64 ? 2 : 1)
     }
     __threadfence();
     __syncthreads();
-    int *counter = p.counters + tile * split + rank;
-    if (tid == 0) last_arrival = atomicAdd(counter, 1) == groups - 1;
+    unsigned long long *counter = p.counters + tile * split + rank;
+    if (tid == 0)
+      last_arrival = arriveCounter(counter, p.epoch, p.err) == static_cast<unsigned>(groups);
     __syncthreads();
     if (!last_arrival) return;
     __threadfence();
@@ -513,6 +516,7 @@ sgblasStatus_t launchSmall(bool ta, bool tb, const kern::GemmParams &gp, const S
   p.ldc = gp.ldc;
   p.alpha = gp.alpha;
   p.beta = gp.beta;
+  p.err = gp.err;
   SmallPlan s = planSmall(gp, sms);
   p.tiles_m = static_cast<int>(s.tiles_m);
   p.slices = s.slices;
@@ -527,20 +531,23 @@ sgblasStatus_t launchSmall(bool ta, bool tb, const kern::GemmParams &gp, const S
     const size_t need =
         kCounterRegionBytes + static_cast<size_t>(s.tiles) * p.groups * tile_bytes;
     unsigned char *base = nullptr;
-    if (counters * sizeof(int) > kCounterRegionBytes) {
+    if (counters * sizeof(Counter) > kCounterRegionBytes) {
       base = nullptr;
     } else if (scratch.fixed != nullptr) {
       if (need <= scratch.fixed_bytes) {
-        if (cudaMemsetAsync(scratch.fixed, 0, counters * sizeof(int), stream) != cudaSuccess)
-          return launchStatus(cudaErrorUnknown);
+        if (!clearFixedCounters(scratch.fixed, counters, stream))
+          return SGBLAS_STATUS_EXECUTION_FAILED;
         base = scratch.fixed;
+        p.epoch = 1;
       }
     } else if (ensureWorkspace(scratch.ctx, need, device, stream)) {
+      p.epoch = nextCounterEpoch(scratch.ctx, stream);
+      if (p.epoch == 0) return SGBLAS_STATUS_EXECUTION_FAILED;
       base = static_cast<unsigned char *>(scratch.ctx->workspace);
       used_handle_workspace = true;
     }
     if (base != nullptr) {
-      p.counters = reinterpret_cast<int *>(base);
+      p.counters = reinterpret_cast<Counter *>(base);
       p.ws = reinterpret_cast<float4 *>(base + kCounterRegionBytes);
     } else {
       p.groups = 1;

@@ -133,7 +133,8 @@ struct GemmParams {
   int sk_tiles;
   int sk_q, sk_r;
   float4 *ws;         // 2 * grid partial-tile slots of Geo::kSlotBytes
-  int *counters;      // sk_tiles arrival counters, zero between launches
+  unsigned long long *counters;   // sk_tiles arrival counters (see arriveCounter)
+  unsigned epoch;                 // this launch's counter epoch (non-zero)
   // cp.async path: floats per copy (1, 2 or 4) allowed by each operand's base
   // alignment and leading dimension.
   int a_vec, b_vec;
@@ -705,7 +706,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         publish(skSlot(p, cta, u));
         __threadfence();
         namedBarrier<1, kThreads>();
-        if (tid == 0) last_arrival = atomicAdd(p.counters + u, 1) == last - first;
+        if (tid == 0)
+          last_arrival = arriveCounter(p.counters + u, p.epoch, p.err) ==
+                         static_cast<unsigned>(last - first + 1);
         namedBarrier<1, kThreads>();
         if (last_arrival) {
           __threadfence();

@@ -37,25 +37,23 @@ Schedule scheduleTf32(t::Tf32Params &q, long long tiles, int slots, int units,
   *used_handle_workspace = false;
   if (s.sk_tiles > 0) {
     const size_t need = kCounterRegionBytes + static_cast<size_t>(slots) * kSlotBytes;
-    const bool counters_fit = static_cast<size_t>(s.sk_tiles) * counters_per_tile * sizeof(int) <=
-                              kCounterRegionBytes;
+    const size_t counters = static_cast<size_t>(s.sk_tiles) * counters_per_tile;
+    const bool counters_fit = counters * sizeof(Counter) <= kCounterRegionBytes;
     unsigned char *base = nullptr;
     if (scratch.fixed != nullptr) {
       if (counters_fit && need <= scratch.fixed_bytes) {
-        if (cudaMemsetAsync(scratch.fixed, 0,
-                            static_cast<size_t>(s.sk_tiles) * counters_per_tile * sizeof(int),
-                            stream) != cudaSuccess) {
-          (void)cudaGetLastError();   // the memset's own error
-          return Schedule{};
-        }
+        if (!clearFixedCounters(scratch.fixed, counters, stream)) return Schedule{};
         base = scratch.fixed;
+        q.epoch = 1;
       }
     } else if (counters_fit && ensureWorkspace(scratch.ctx, need, device, stream)) {
+      q.epoch = nextCounterEpoch(scratch.ctx, stream);
+      if (q.epoch == 0) return Schedule{};
       base = static_cast<unsigned char *>(scratch.ctx->workspace);
       *used_handle_workspace = true;
     }
     if (base != nullptr) {
-      q.counters = reinterpret_cast<int *>(base);
+      q.counters = reinterpret_cast<Counter *>(base);
       q.ws = reinterpret_cast<float *>(base + kCounterRegionBytes);
     } else {
       s = Schedule{};

@@ -83,7 +83,8 @@ struct Tf32Params {
   // over all CTAs (stream-K), pieces summed in order by the last arriver.
   int grid, dp_tiles, sk_tiles, sk_q, sk_r;
   float *ws;          // 2 * grid piece slots of 128 x N floats
-  int *counters;      // sk_tiles arrival counters, zero between launches
+  unsigned long long *counters;   // sk_tiles arrival counters (see arriveCounter)
+  unsigned epoch;                 // this launch's counter epoch (non-zero)
 };
 
 // Shared-memory matrix descriptor (tcgen05), version 1.
@@ -306,7 +307,9 @@ __global__ void __launch_bounds__(kThreads, 1) tf32Kernel(const __grid_constant_
       const int last = skOwner(p, (u + 1) * p.kiters - 1);
       __threadfence();
       namedBarrier<1, 128>();
-      if (etid == 0) last_arrival = atomicAdd(p.counters + u, 1) == last - first;
+      if (etid == 0)
+        last_arrival = arriveCounter(p.counters + u, p.epoch, p.err) ==
+                       static_cast<unsigned>(last - first + 1);
       namedBarrier<1, 128>();
       if (last_arrival) {
         __threadfence();
@@ -610,10 +613,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbarArriveCluster(clusterAddr(smemAddr(&acc_empty[b]), 0));
       const int first = skOwner(p, u * p.kiters);
       const int last = skOwner(p, (u + 1) * p.kiters - 1);
-      int *counter = p.counters + 2 * u + static_cast<int>(rank);
+      unsigned long long *counter = p.counters + 2 * u + static_cast<int>(rank);
       __threadfence();
       namedBarrier<1, 128>();
-      if (etid == 0) last_arrival = atomicAdd(counter, 1) == last - first;
+      if (etid == 0)
+        last_arrival = arriveCounter(counter, p.epoch, p.err) ==
+                       static_cast<unsigned>(last - first + 1);
       namedBarrier<1, 128>();
       if (last_arrival) {
         __threadfence();

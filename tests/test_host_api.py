@@ -44,6 +44,23 @@ def test_library_exports_every_declared_symbol():
     assert set(sg.EXPORTED_SYMBOLS) >= set(names) - set(), "ctypes table incomplete"
 
 
+def test_library_exports_only_the_c_api():
+    """Nothing but the declared C API leaves the library: no C++ template
+    instances, kernel stubs or CUDA-runtime symbols, and in particular no
+    STB_GNU_UNIQUE objects, which the dynamic linker merges across every
+    library of the process even under RTLD_LOCAL (two copies of the library
+    would then share their per-kernel set-up flags)."""
+    out = subprocess.run(["readelf", "--dyn-syms", "-W", str(sg.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    defined = []
+    for line in out.splitlines():
+        f = line.split()
+        if len(f) >= 8 and f[6] != "UND" and f[4] in ("GLOBAL", "WEAK", "UNIQUE"):
+            defined.append((f[4], f[7].split("@")[0]))
+    assert not [n for b, n in defined if b == "UNIQUE"], "GNU_UNIQUE symbols exported"
+    assert sorted(n for _, n in defined) == declared_symbols()
+
+
 def test_create_destroy_contract():
     assert sg.lib.sgblasCreate(None) == sg.SGBLAS_STATUS_INVALID_VALUE
     assert sg.lib.sgblasDestroy(None) == sg.SGBLAS_STATUS_NOT_INITIALIZED

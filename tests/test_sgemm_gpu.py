@@ -287,6 +287,58 @@ def test_one_handle_many_stream_k_shapes(cuda, handle):
         _assert(check_sampled(case, a, b, c, out, count=8192, seed=i), (i, m, n, k))
 
 
+def test_split_products_exact_after_interrupted_launch(cuda, handle):
+    """A split launch that stops early (a bounded wait that timed out) leaves
+    its arrival counters part-counted. sgblasTestInterruptScratch puts the
+    handle's counters in exactly that state; the next split product on the
+    same handle -- FP32 tile kernel, cluster kernel with several clusters
+    per tile, TF32 lane -- must still be exact and bit-identical to the
+    product before it. Then a captured graph of a split product is replayed
+    three times (each replay reuses one epoch; the last arrival of each tile
+    resets its counter)."""
+    import ctypes
+    torch = cuda
+    shapes = [("fp32", 1500, 1300, 3000), ("fp32", 128, 128, 8192), ("tf32", 1024, 1024, 4096)]
+    try:
+        for math, m, n, k in shapes:
+            handle.set_math_mode(sg.SGBLAS_MATH_TF32 if math == "tf32" else sg.SGBLAS_MATH_FP32)
+            case = C.Case("interrupt", 0, 0, m, n, k, m, k, m, 1.0, 0.5)
+            a, b, c = C.cfg_inputs(case, 313, None)
+            status, first = run_sgemm(torch, handle, case, a, b, c)
+            assert status == 0
+            assert sg.lib.sgblasTestInterruptScratch(handle.raw) == 0
+            status, again = run_sgemm(torch, handle, case, a, b, c)
+            assert status == 0
+            assert np.array_equal(first, again), (math, m, n, k)
+            if math == "fp32":
+                _assert(check_sampled(case, a, b, c, again, count=8192), (m, n, k))
+    finally:
+        handle.set_math_mode(sg.SGBLAS_MATH_FP32)
+    case = C.Case("graph-sk", 0, 0, 1500, 1300, 3000, 1500, 3000, 1500, 1.0, 0.0)
+    a, b, c = C.cfg_inputs(case, 314, None)
+    _, expect = run_sgemm(torch, handle, case, a, b, c)
+    da, pa = to_device(torch, a)
+    db, pb = to_device(torch, b)
+    dc, pc = to_device(torch, c)
+    stream = torch.cuda.Stream()
+    handle.set_stream(stream)
+    try:
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            handle.sgemm(0, 0, case.m, case.n, case.k, 1.0, pa, case.lda, pb, case.ldb, 0.0, pc,
+                         case.ldc)
+        for _ in range(3):
+            dc.fill_(float("nan"))
+            graph.replay()
+            torch.cuda.synchronize()
+            assert np.array_equal(dc.cpu().numpy(), expect)
+        del graph
+    finally:
+        handle.set_stream(None)
+    assert sg.get_device_errors() == 0
+
+
 def test_matches_reference_golden_outputs(cuda, handle):
     """Our outputs at the entries the reference library produced on a B200
     (tests/golden/reference_suite.npz): both lie within the north-star bound
