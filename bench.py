@@ -70,6 +70,11 @@ def parse_args():
                     help="N=1: matrices per call (sgblasSgemmStridedBatched when > 1)")
     ap.add_argument("--no-flush", action="store_true",
                     help="N=1: back-to-back calls without the L2 flush (latency of small calls)")
+    ap.add_argument("--back-to-back", type=int, default=0, metavar="R",
+                    help="N=1: R calls between one pair of events per step, no L2 flush (the "
+                         "reference benchmark's protocol, bench/benchmark.cu:290-307)")
+    ap.add_argument("--no-sharded-n1", action="store_true",
+                    help="N=1: skip the config-5 (32768 x 32768 x 8192) single-GPU line")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
@@ -132,7 +137,7 @@ class ClockSampler:
         # median of the busy samples (the region is bracketed by idle time)
         busy = [s for s in sm if s >= 0.5 * max(sm)] or sm
         return {"sm_mhz": statistics.median(busy), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "busy_samples": len(busy)}
 
 
 def smi_index(torch, dev: int) -> str:
@@ -228,11 +233,111 @@ def cpu_baseline(a, b, m, n, k, lda, ldb, budget_s: float) -> dict:
     oracle.sgemm_cpu(0, 0, m, k, 1.0, a, lda, b, ldb, 0.0, c, m, 0, cols, threads)
     dt = time.perf_counter() - t0
     rate = 2.0 * m * k * cols / dt / 1e12
+    # One thread, the reference's loop order exactly (column, row, k).
+    c1 = np.zeros(m, dtype=np.float32)
+    t0 = time.perf_counter()
+    one_cols = 0
+    while one_cols < n and (one_cols == 0 or time.perf_counter() - t0 < budget_s / 4):
+        oracle.sgemm_cpu(0, 0, m, k, 1.0, a, lda, b, ldb, 0.0, c1, m, one_cols, one_cols + 1, 1)
+        one_cols += 1
+    dt1 = time.perf_counter() - t0
     return {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"columns 0..{cols - 1} of C ({cols}/{n}) of the {m}x{n}x{k} NN workload, "
                       f"FP64-accumulated oracle loop of tests/cuda/correctness.cu:373-392, "
                       f"{dt:.1f} s, rate extrapolated per column",
-            "seconds": dt}
+            "seconds": dt, "cpu_model": cpu_model(),
+            "single_thread": {"value": 2.0 * m * k * one_cols / dt1 / 1e12, "unit": UNIT,
+                              "cores": 1, "seconds": dt1,
+                              "sample": f"{one_cols} columns of C, one thread, the reference "
+                                        "loop order (column, row, k)"}}
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+def sampled_parity(torch, a, b, c, m, n, k, lda, ldb, ldc, alpha=1.0, count=4096, seed=0,
+                   full_cols=(0, -1)) -> dict:
+    """Sampled check of an NN product with beta = 0 against an FP64
+    restatement of the oracle loop (tests/cuda/correctness.cu:373-392): C at
+    `count` random entries plus every row of the columns in full_cols (-1:
+    the last column), within the north-star bound 2*max(K,2)*2^-24*mag,
+    mag = |alpha| * sum |a*b|. Runs after timing, on the GPU in FP64 (torch
+    reductions; nothing of this library is involved)."""
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    rows = torch.randint(0, m, (count,), generator=g).to(a.device)
+    cols = torch.randint(0, n, (count,), generator=g).to(a.device)
+    av = a[: lda * k].view(k, lda)
+    bv = b[: ldb * n].view(n, ldb)[:, :k]
+    cv = c[: ldc * n].view(n, ldc)
+    ar = av[:, rows].double().T            # count x k
+    bc = bv[cols].double()                 # count x k
+    ref = alpha * (ar * bc).sum(1)
+    mag = abs(alpha) * (ar.abs() * bc.abs()).sum(1)
+    got = cv[cols, rows].double()
+    ratio = ((got - ref).abs() / (2.0 * max(k, 2) * 2.0 ** -24 * mag).clamp_min(1e-300)).max()
+    worst = float(ratio)
+    finite = bool(torch.isfinite(got).all())
+    a64 = av[:, :m].double()               # k x m
+    checked = count
+    for j in full_cols:
+        j = n - 1 if j < 0 else j
+        col = bv[j].double()
+        ref = alpha * (a64.T @ col)
+        mag = abs(alpha) * (a64.abs().T @ col.abs())
+        got = cv[j, :m].double()
+        worst = max(worst, float(((got - ref).abs() /
+                                  (2.0 * max(k, 2) * 2.0 ** -24 * mag).clamp_min(1e-300)).max()))
+        finite = finite and bool(torch.isfinite(got).all())
+        checked += m
+    del a64
+    return {"checked": checked, "max_ratio": worst, "ok": finite and worst <= 1.0,
+            "method": f"{count} random entries + every row of columns {list(full_cols)}, FP64, "
+                      "bound 2*max(K,2)*2^-24*|alpha|*sum|a*b|"}
+
+
+def sharded_n1(torch, sg, steps: int, warmup: int) -> dict:
+    """BASELINE configs[4] on one GPU: 32768 x 32768 x 8192 NN, alpha 1, beta
+    0, one sgblasSgemm per step (what the sharded path runs with one rank);
+    inputs (6 GiB) larger than L2. The denominator of the multi-GPU scaling."""
+    M, N, K = 32768, 32768, 8192
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    a = torch.empty(M * K, device="cuda").uniform_(-1.0, 1.0, generator=gen)
+    b = torch.empty(K * N, device="cuda").uniform_(-1.0, 1.0, generator=gen)
+    c = torch.empty(M * N, device="cuda")
+    stream = torch.cuda.Stream()
+    h = sg.Handle()
+    h.set_stream(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            h.sgemm(0, 0, M, N, K, 1.0, a, M, b, K, 0.0, c, M)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    with torch.cuda.stream(stream):
+        for i in range(steps):
+            ev[i][0].record(stream)
+            h.sgemm(0, 0, M, N, K, 1.0, a, M, b, K, 0.0, c, M)
+            ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    secs = sum(s.elapsed_time(e) for s, e in ev) / 1e3
+    h.close()
+    parity = sampled_parity(torch, a, b, c, M, N, K, M, K, M)
+    del a, b, c
+    torch.cuda.empty_cache()
+    return {"value": 2.0 * M * N * K * steps / secs / 1e12, "unit": UNIT,
+            "ms_per_step": 1e3 * secs / steps, "steps": steps, "warmup": warmup,
+            "workload": f"sgemm NN {M}x{N}x{K} alpha=1 beta=0 on one GPU (BASELINE configs[4] "
+                        "unsharded); inputs larger than L2", "parity": parity}
 
 
 # ---------------------------------------------------------------------------
@@ -331,6 +436,10 @@ def run_single(args) -> None:
             h.sgemm_strided_batched(ta, tb, m, n, k, alpha, da, lda, sa, db, ldb, sb, beta, dc,
                                     ldc, sc, batch)
 
+    reps = max(1, args.back_to_back)
+    if args.back_to_back:
+        args.no_flush = True
+
     def flush_l2():
         if not args.no_flush:
             flush.zero_()
@@ -349,11 +458,12 @@ def run_single(args) -> None:
             for i in range(steps):
                 flush_l2()
                 ev[i][0].record(stream)
-                launch()
+                for _ in range(reps):
+                    launch()
                 ev[i][1].record(stream)
         torch.cuda.synchronize()
     times_ms = [s.elapsed_time(e) for s, e in ev]
-    total_s = sum(times_ms) / 1e3
+    total_s = sum(times_ms) / 1e3 / reps      # per call
     value = flops * steps / total_s / 1e12
     clocks = clk.summary()
     if sg.get_device_errors() != 0:
@@ -362,7 +472,8 @@ def run_single(args) -> None:
     mhz = clocks["sm_mhz"] or 1965.0
     peak = fp32_peak_tflops(sms, mhz)
     peak_source = (f"{sms} SMs x {FP32_LANES_PER_SM} FP32 lanes x 2 x {mhz:.0f} MHz "
-                   "(median SM clock sampled during the timed region); "
+                   f"(median of {clocks.get('busy_samples', 0)} busy SM-clock samples of "
+                   f"{clocks.get('samples', 0)} taken during the timed region); "
                    "MEASURED_PEAKS.json has no FP32 CUDA-core figure")
     if tf32:
         measured = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
@@ -402,7 +513,8 @@ def run_single(args) -> None:
                       "l2": ("not flushed: back-to-back calls" if args.no_flush else
                              "flushed before every timed step (256 MiB write outside the "
                              "step's CUDA events)")},
-           "roofline": roofline, "clocks": clocks, "gpu_launches": steps,
+           "calls_per_event_pair": reps,
+           "roofline": roofline, "clocks": clocks, "gpu_launches": steps * reps,
            "device": props.name}
 
     if not args.no_cublas:
@@ -426,11 +538,12 @@ def run_single(args) -> None:
                 for i in range(steps):
                     flush_l2()
                     cev[i][0].record(stream)
-                    st = cublas_call()
+                    for _ in range(reps):
+                        st = cublas_call()
                     cev[i][1].record(stream)
             torch.cuda.synchronize()
             assert st == 0
-            cval = flops * steps / (sum(s.elapsed_time(e) for s, e in cev) / 1e3) / 1e12
+            cval = flops * steps * reps / (sum(s.elapsed_time(e) for s, e in cev) / 1e3) / 1e12
             out["cublas_tf32" if tf32 else "cublas_pedantic"] = {
                 "value": cval, "unit": UNIT, "ratio": value / cval, "version": cb.version,
                 "call": ("cublasGemmEx" if batch == 1 else "cublasGemmStridedBatchedEx") +
@@ -441,8 +554,12 @@ def run_single(args) -> None:
         except (OSError, AssertionError) as e:
             out["cublas_pedantic"] = {"unavailable": str(e)}
 
+    if plain and beta == 0.0:
+        out["parity"] = sampled_parity(torch, da, db, dc, m, n, k, lda, ldb, ldc)
     if not args.no_e2e and plain:
         out["e2e"] = e2e_single(torch, sg, ha, hb, hc, beta, m, n, k, max(10, steps // 4), warmup)
+    if not args.no_sharded_n1 and plain and (m, n, k, beta) == (4096, 4096, 4096, 0.0):
+        out["sharded_n1"] = sharded_n1(torch, sg, 3, 3)
     if not args.no_cpu_baseline and plain:
         out["cpu_baseline"] = cpu_baseline(ha, hb, m, n, k, lda, ldb, args.cpu_seconds)
     h.close()
@@ -515,7 +632,7 @@ def run_sharded(args) -> None:
     from datetime import timedelta
 
     import sgblas_b200 as sg
-    from sgblas_b200.mg import check_consistent, exchange_unique_id, shard_columns
+    from sgblas_b200.mg import check_consistent, exchange_unique_id, panel_plan, shard_columns
 
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
@@ -534,9 +651,9 @@ def run_sharded(args) -> None:
 
     gen = torch.Generator(device="cuda")
     gen.manual_seed(5 + rank)
-    a = torch.empty(M * K, device="cuda")
-    if rank == 0:
-        a.uniform_(-1.0, 1.0, generator=gen)
+    # A exists on the root only; the call sends it to the other ranks' staging.
+    a = torch.empty(M * K, device="cuda").uniform_(-1.0, 1.0, generator=gen) if rank == 0 \
+        else None
     b = torch.empty(K * n_loc, device="cuda").uniform_(-1.0, 1.0, generator=gen)
     c = torch.empty(M * n_loc, device="cuda")
 
@@ -569,7 +686,21 @@ def run_sharded(args) -> None:
     allc = [None] * world
     dist.all_gather_object(allc, clocks)
     errors = sg.get_device_errors()
-    del a, b, c
+    # Parity of the timed steps' C (outside the timed region): one more call
+    # with no columns of its own delivers A to every rank (C untouched), then
+    # each rank checks its shard against FP64.
+    a_full = a if rank == 0 else torch.empty(M * K, device="cuda")
+    with torch.cuda.stream(stream):
+        mg.sgemm(0, 0, M, 0, K, 1.0, a_full, M, 0, b, K, 0.0, c, M)
+    torch.cuda.synchronize()
+    mine = sampled_parity(torch, a_full, b, c, M, n_loc, K, M, K, M, seed=rank)
+    parities = [None] * world
+    dist.all_gather_object(parities, mine)
+    parity = {"checked": sum(x["checked"] for x in parities),
+              "max_ratio": max(x["max_ratio"] for x in parities),
+              "ok": all(x["ok"] for x in parities),
+              "method": "every rank: " + mine["method"] + "; A delivered by a further call"}
+    del a, b, c, a_full
     torch.cuda.empty_cache()
 
     e2e = None
@@ -589,16 +720,22 @@ def run_sharded(args) -> None:
                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                "config": {"workload": f"sharded sgemm NN {M}x{N}x{K} (BASELINE configs[4]), "
                                       f"B and C split into {world} column blocks, "
-                                      "A (1 GiB) broadcast from rank 0 by NCCL in every step",
+                                      "A (1 GiB) sent from rank 0 to every rank in every step",
                           "m": M, "n": N, "k": K,
-                          "parallelism": f"column-shard x{world}", "l2": "inputs larger than L2"},
+                          "parallelism": f"column-shard x{world}", "l2": "inputs larger than L2",
+                          "broadcast": "A sent along a chain of ranks by copy engines in row "
+                                       "panels (512, 1024, 2048, ~4096 rows), each rank "
+                                       "computing a panel's rows as it arrives"},
+               "parity": parity,
                "roofline": {"bound": "fp32_fma", "achieved": value, "peak": peak, "unit": UNIT,
                             "frac": value / peak, "traffic": None,
                             "peak_source": f"{world} x {sms} SMs x 128 lanes x 2 x {mhz:.0f} MHz "
                                            "(median sampled SM clock)"},
                "clocks": {"sm_mhz": mhz, "sm_max_mhz": max((x["sm_max_mhz"] or 0) for x in allc),
                           "reasons": reasons},
-               "gpu_launches": steps, "e2e": e2e}
+               "gpu_launches": steps * len(panel_plan(M, K, world)),
+               "gpu_launches_note": "per rank: one product kernel per row panel of A per step",
+               "e2e": e2e}
         emit(json.dumps(out))
     dist.barrier()
     dist.destroy_process_group()
@@ -611,8 +748,9 @@ def e2e_sharded(torch, dist, sg, mg, rank, M, n_loc, K, flops, steps) -> dict:
     pa = torch.empty(M * K).uniform_(-1.0, 1.0).pin_memory() if rank == 0 else None
     pb = torch.empty(K * n_loc).uniform_(-1.0, 1.0).pin_memory()
     pc = torch.empty(M * n_loc).pin_memory()
-    sets = [(torch.empty(M * K, device="cuda"), torch.empty(K * n_loc, device="cuda"),
-             torch.empty(M * n_loc, device="cuda")) for _ in range(2)]
+    sets = [(torch.empty(M * K, device="cuda") if rank == 0 else None,
+             torch.empty(K * n_loc, device="cuda"), torch.empty(M * n_loc, device="cuda"))
+            for _ in range(2)]
     s_in, s_comp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
     mg.set_stream(s_comp)
     in_done = [torch.cuda.Event() for _ in range(2)]

@@ -79,6 +79,7 @@ _SIGNATURES = {
     "sgblasMgCreate": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
                                        ctypes.c_void_p, ctypes.c_int]),
     "sgblasMgDestroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "sgblasMgAbort": (ctypes.c_int, [ctypes.c_void_p]),
     "sgblasMgSetStream": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "sgblasMgSetMathMode": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "sgblasMgGetRank": (ctypes.c_int, [ctypes.c_void_p, _c_int_p, _c_int_p]),
@@ -235,10 +236,14 @@ class MgHandle:
         _check("sgblasMgCreate", lib.sgblasMgCreate(ctypes.byref(raw), nranks, rank, uid, device))
         self._h = raw
 
-    def close(self) -> None:
+    def close(self) -> int:
+        """sgblasMgDestroy; returns its status (EXECUTION_FAILED after an
+        abort, or when work was still waiting for a peer at the deadline)."""
+        status = SGBLAS_STATUS_SUCCESS
         if self._h is not None and self._h.value is not None:
-            _check("sgblasMgDestroy", lib.sgblasMgDestroy(self._h))
+            status = lib.sgblasMgDestroy(self._h)
         self._h = None
+        return status
 
     def set_math_mode(self, mode: int) -> None:
         _check("sgblasMgSetMathMode", lib.sgblasMgSetMathMode(self._h, mode))
@@ -254,6 +259,9 @@ class MgHandle:
 
     def sgemm(self, *args) -> None:
         _check("sgblasMgSgemm", self.sgemm_status(*args))
+
+    def abort(self) -> None:
+        _check("sgblasMgAbort", lib.sgblasMgAbort(self._h))
 
     def all_gather(self, send, recv, count: int) -> None:
         _check("sgblasMgAllGather", lib.sgblasMgAllGather(self._h, _ptr(send), _ptr(recv), count))

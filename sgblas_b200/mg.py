@@ -9,7 +9,10 @@ C entry point ``sgblasMgSgemm``, and need no GPU (they are tested with
 * :func:`exchange_unique_id` -- rank 0 creates the NCCL id, every rank gets it.
 * :func:`check_consistent` -- before entering the collective, every rank's
   problem-wide arguments are compared on the host; a mismatch raises on every
-  rank instead of leaving NCCL ranks waiting for a broadcast that never comes.
+  rank instead of leaving ranks waiting for panels of A that never come.
+* :func:`panel_plan` -- the row panels in which sgblasMgSgemm sends A (one
+  product launch per panel per rank), the rule of planPanels in
+  csrc/mg.cu.
 """
 from __future__ import annotations
 
@@ -56,3 +59,32 @@ def check_consistent(args: dict, group=None) -> None:
 
 def shard_sizes(n: int, world: int) -> Sequence[int]:
     return [shard_columns(n, world, r)[1] for r in range(world)]
+
+
+PANEL_SPLIT_BYTES = 32 << 20
+MAX_PANELS = 16
+
+
+def panel_plan(m: int, k: int, nranks: int) -> list[tuple[int, int]]:
+    """(first row, rows) of each panel of op(A) (m x k floats) that
+    sgblasMgSgemm sends along the chain: one panel for one rank, a small A
+    (< 32 MiB) or m < 1024; else 512, 1024 and 2048 rows while at least twice
+    that many rows remain, then the rest in at most 16 - (ramp panels)
+    near-equal panels of about 4096 rows, rounded up to multiples of 128."""
+    if nranks == 1 or m * k * 4 < PANEL_SPLIT_BYTES or m < 1024:
+        return [(0, m)]
+    out, at, rows = [], 0, 512
+    while rows <= 2048 and m - at >= 2 * rows:
+        out.append((at, rows))
+        at += rows
+        rows *= 2
+    rest = m - at
+    count = max(1, min(MAX_PANELS - len(out), (rest + 4095) // 4096))
+    step = (rest // count + 127) // 128 * 128
+    for i in range(count):
+        if at >= m:
+            break
+        take = m - at if i == count - 1 else min(step, m - at)
+        out.append((at, take))
+        at += take
+    return out
