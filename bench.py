@@ -72,7 +72,9 @@ def parse_args():
                     help="N=1: back-to-back calls without the L2 flush (latency of small calls)")
     ap.add_argument("--back-to-back", type=int, default=0, metavar="R",
                     help="N=1: R calls between one pair of events per step, no L2 flush (the "
-                         "reference benchmark's protocol, bench/benchmark.cu:290-307)")
+                         "reference benchmark's protocol, bench/benchmark.cu:290-307); the R "
+                         "calls are captured once in a CUDA graph and replayed, for ours and "
+                         "for cuBLAS alike, so that no host overhead sits between them")
     ap.add_argument("--no-sharded-n1", action="store_true",
                     help="N=1: skip the config-5 (32768 x 32768 x 8192) single-GPU line")
     ap.add_argument("--no-e2e", action="store_true")
@@ -234,7 +236,7 @@ def cpu_baseline(a, b, m, n, k, lda, ldb, budget_s: float) -> dict:
     dt = time.perf_counter() - t0
     rate = 2.0 * m * k * cols / dt / 1e12
     # One thread, the reference's loop order exactly (column, row, k).
-    c1 = np.zeros(m, dtype=np.float32)
+    c1 = np.zeros(m * n, dtype=np.float32)    # column j is written at c1[j * m]
     t0 = time.perf_counter()
     one_cols = 0
     while one_cols < n and (one_cols == 0 or time.perf_counter() - t0 < budget_s / 4):
@@ -450,6 +452,17 @@ def run_single(args) -> None:
             launch()
     torch.cuda.synchronize()
 
+    def capture(fn):
+        # The R back-to-back calls as one CUDA graph (set-up done by warm-up).
+        graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(reps):
+                fn()
+        torch.cuda.synchronize()
+        return graph
+
+    graph = capture(launch) if args.back_to_back else None
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(steps)]
     with ClockSampler(smi_index(torch, dev)) as clk:
@@ -458,7 +471,9 @@ def run_single(args) -> None:
             for i in range(steps):
                 flush_l2()
                 ev[i][0].record(stream)
-                for _ in range(reps):
+                if graph is not None:
+                    graph.replay()
+                else:
                     launch()
                 ev[i][1].record(stream)
         torch.cuda.synchronize()
@@ -514,6 +529,8 @@ def run_single(args) -> None:
                              "flushed before every timed step (256 MiB write outside the "
                              "step's CUDA events)")},
            "calls_per_event_pair": reps,
+           "launch": ("the calls of a step replayed as one CUDA graph" if args.back_to_back
+                      else "one call per step from the host"),
            "roofline": roofline, "clocks": clocks, "gpu_launches": steps * reps,
            "device": props.name}
 
@@ -530,15 +547,21 @@ def run_single(args) -> None:
                                                 db.data_ptr(), ldb, sb, beta, dc2.data_ptr(), ldc,
                                                 sc, batch)
 
-            for _ in range(warmup):
-                cublas_call()
+            with torch.cuda.stream(stream):
+                for _ in range(warmup):
+                    st = cublas_call()
+            torch.cuda.synchronize()
+            assert st == 0
+            cgraph = capture(cublas_call) if args.back_to_back else None
             cev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(steps)]
             with torch.cuda.stream(stream):
                 for i in range(steps):
                     flush_l2()
                     cev[i][0].record(stream)
-                    for _ in range(reps):
+                    if cgraph is not None:
+                        cgraph.replay()
+                    else:
                         st = cublas_call()
                     cev[i][1].record(stream)
             torch.cuda.synchronize()

@@ -41,7 +41,8 @@ sgblasStatus_t sgblasTestInterruptScratch(sgblasHandle_t handle);
  * built into the library, which every GPU that loads the library holds until
  * exit. It never calls cudaMalloc, cudaFree or any allocating routine.
  *   - The first call on a device resolves the scratch address; make it
- *     before any stream capture.
+ *     before any stream capture. After cudaDeviceReset the next call
+ *     resolves it again (make that one before any capture too).
  *   - All calls on a device share the scratch and it keeps the last call's
  *     contents: calls that may overlap on the GPU race, so order them.
  *   - A schedule that needs more scratch than 38 MiB (only possible on a GPU

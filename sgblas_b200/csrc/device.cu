@@ -2,6 +2,10 @@
 #include "device.hpp"
 #include "ptx.cuh"
 
+#include <cuda.h>
+
+#include <new>
+
 #include <sgblas/sgblas_ext.h>
 
 namespace sgblas::detail {
@@ -9,21 +13,60 @@ namespace {
 
 __device__ unsigned g_device_error;
 
-std::atomic<unsigned *> g_error_word[kMaxDevices];
+SymbolCache g_error_word;
+
+struct SymbolEntry {
+  void *context;
+  void *address;
+};
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+
+// The calling thread's current context, or nullptr (none yet, or the driver
+// entry point is unavailable).
+void *currentContext() {
+  static const CtxGetCurrentFn fn = [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      (void)cudaGetLastError();
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    }
+    return reinterpret_cast<CtxGetCurrentFn>(f);
+  }();
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
 
 }  // namespace
 
-unsigned *deviceErrorWord(int device) {
+void *symbolAddress(SymbolCache *cache, int device, const void *symbol) {
   if (device < 0 || device >= kMaxDevices) return nullptr;
-  unsigned *cached = g_error_word[device].load(std::memory_order_acquire);
-  if (cached != nullptr) return cached;
+  const void *context = currentContext();
+  const auto *entry =
+      static_cast<const SymbolEntry *>(cache->entry[device].load(std::memory_order_acquire));
+  if (entry != nullptr && context != nullptr && entry->context == context) return entry->address;
   void *address = nullptr;
-  if (cudaGetSymbolAddress(&address, g_device_error) != cudaSuccess) {
+  if (cudaGetSymbolAddress(&address, symbol) != cudaSuccess) {   // makes the context current
     (void)cudaGetLastError();
     return nullptr;
   }
-  g_error_word[device].store(static_cast<unsigned *>(address), std::memory_order_release);
-  return static_cast<unsigned *>(address);
+  context = currentContext();
+  if (context != nullptr) {
+    // Published once per (device, context); an entry replaced by a newer
+    // one is left allocated (a few bytes per context change), so a reader
+    // holding it never sees freed memory.
+    auto *fresh = new (std::nothrow) SymbolEntry{const_cast<void *>(context), address};
+    if (fresh != nullptr) cache->entry[device].store(fresh, std::memory_order_release);
+  }
+  return address;
+}
+
+unsigned *deviceErrorWord(int device) {
+  return static_cast<unsigned *>(symbolAddress(&g_error_word, device, &g_device_error));
 }
 
 namespace {

@@ -14,6 +14,17 @@ namespace sgblas::detail {
 
 constexpr int kMaxDevices = 64;
 
+// A device address of a __device__ symbol, cached per device and keyed on
+// the CUDA context that was current when it was looked up: after the
+// context is replaced (cudaDeviceReset, then the next runtime call makes a
+// new primary context with the modules loaded again) the address is looked
+// up anew instead of pointing into freed memory.
+struct SymbolCache {
+  std::atomic<const void *> entry[kMaxDevices];   // a SymbolEntry, never freed
+};
+// Address of `symbol` on `device` (the current device), or nullptr.
+void *symbolAddress(SymbolCache *cache, int device, const void *symbol);
+
 // Address of the device error word on `device` (the current device), or
 // nullptr if it cannot be resolved. Kernels OR error codes into it
 // (kern::kErrBarrierTimeout, ...); the host reads it with

@@ -13,7 +13,9 @@
 // three differences:
 //   - The first call on a device looks up the scratch array's device address
 //     (cudaGetSymbolAddress, with that device current) and caches it. Make
-//     that first call before any stream capture.
+//     that first call before any stream capture. The cache is keyed on the
+//     current CUDA context, so after cudaDeviceReset the next call looks the
+//     address up again (make it, too, before any capture).
 //   - All calls on a device share the one scratch array, and it keeps what the
 //     last call left in it. Calls whose kernels can overlap on the GPU (e.g.
 //     issued on two streams without ordering) race on it: order them.
@@ -51,20 +53,15 @@ static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
 namespace {
 
-// Device address of g_scratch per device. In host code `g_scratch` only names
-// a host-side stand-in, so its address must come from cudaGetSymbolAddress.
-std::atomic<unsigned char *> g_scratch_address[sgblas::detail::kMaxDevices];
+// Device address of g_scratch per device (and per context: looked up again
+// after cudaDeviceReset). In host code `g_scratch` only names a host-side
+// stand-in, so its address must come from cudaGetSymbolAddress, called with
+// the device current.
+sgblas::detail::SymbolCache g_scratch_address;
 
 unsigned char *scratchAddress(int device) {
-  if (device < 0 || device >= sgblas::detail::kMaxDevices) return nullptr;
-  unsigned char *ptr = g_scratch_address[device].load(std::memory_order_acquire);
-  if (ptr != nullptr) return ptr;
-  if (cudaGetSymbolAddress(reinterpret_cast<void **>(&ptr), g_scratch) != cudaSuccess) {
-    (void)cudaGetLastError();
-    return nullptr;
-  }
-  g_scratch_address[device].store(ptr, std::memory_order_release);
-  return ptr;
+  return static_cast<unsigned char *>(
+      sgblas::detail::symbolAddress(&g_scratch_address, device, &g_scratch));
 }
 
 }  // namespace

@@ -6,13 +6,39 @@ import numpy as np
 import oracle
 
 
+# Guard bands: every operand sits between two 64 KiB bands of a sentinel bit
+# pattern (a NaN), in place of compute-sanitizer's bounds checking: a read
+# outside an operand picks up NaN (which the oracle comparison rejects), and a
+# write outside it changes a band (check_guards).
+GUARD_FLOATS = 16384
+GUARD_BITS = 0x7F8C0DE5
+
+
 def to_device(torch, host: np.ndarray, offset: int = 0):
     """Copy a float32 array to the GPU; offset > 0 places it `offset` floats
-    into a larger buffer (for misaligned-pointer cases). Returns (buffer,
-    device address of element 0)."""
-    buf = torch.empty(host.size + offset, dtype=torch.float32, device="cuda")
+    into the buffer (for misaligned-pointer cases). Returns (buffer, device
+    address of element 0): buffer[offset:] is the array. The buffer sits
+    between guard bands (the offset gap belongs to the band before it)."""
+    g = GUARD_FLOATS
+    full = torch.empty(g + offset + host.size + g, dtype=torch.float32, device="cuda")
+    full.view(torch.int32).fill_(GUARD_BITS - (1 << 32) if GUARD_BITS >= 1 << 31 else GUARD_BITS)
+    buf = full[g:g + offset + host.size]
     buf[offset:].copy_(torch.from_numpy(np.ascontiguousarray(host)))
+    buf._sg_guard = (full, g + offset, g + offset + host.size)
     return buf, buf.data_ptr() + 4 * offset
+
+
+def check_guards(*bufs) -> None:
+    """Asserts that the guard bands around each to_device buffer still hold
+    the sentinel bits: nothing was written before or after the operand."""
+    for i, buf in enumerate(bufs):
+        full, lo, hi = buf._sg_guard
+        bits = full.view(full.dtype).cpu().numpy().view(np.uint32)
+        bad_lo = np.flatnonzero(bits[:lo] != GUARD_BITS)
+        bad_hi = np.flatnonzero(bits[hi:] != GUARD_BITS)
+        assert bad_lo.size == 0 and bad_hi.size == 0, (
+            f"operand {i}: {bad_lo.size} floats written before it (nearest {lo - bad_lo.max() if bad_lo.size else 0} "
+            f"floats before), {bad_hi.size} after it (first at +{bad_hi.min() if bad_hi.size else 0})")
 
 
 def run_sgemm(torch, handle, case, a, b, c, offsets=(0, 0, 0), stream=None):
@@ -26,6 +52,7 @@ def run_sgemm(torch, handle, case, a, b, c, offsets=(0, 0, 0), stream=None):
     status = handle.sgemm_status(case.transa, case.transb, case.m, case.n, case.k, case.alpha, pa,
                                  case.lda, pb, case.ldb, case.beta, pc, case.ldc)
     torch.cuda.synchronize()
+    check_guards(da, db, dc)
     out = dc[offsets[2]:].cpu().numpy()
     if stream is not None:
         handle.set_stream(None)

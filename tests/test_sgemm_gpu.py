@@ -17,7 +17,7 @@ import pytest
 import oracle
 import sgblas_b200 as sg
 from tests import cases as C
-from tests.gpu_util import c_view, check_full, check_sampled, run_sgemm, to_device
+from tests.gpu_util import c_view, check_full, check_guards, check_sampled, run_sgemm, to_device
 
 pytestmark = pytest.mark.gpu
 
@@ -167,6 +167,7 @@ def test_copy_staging_without_workspace(cuda, handle, ta, tb, m, n, k, pad, offs
                                            lda, pb, ldb, ctypes.byref(f(beta)), pc, ldc)
         torch.cuda.synchronize()
         assert status == 0
+        check_guards(da, db, dc)
         out = dc[offs[2]:].cpu().numpy()
         _assert(check_full(case, a, b, c, out), (ta, tb, m, n, k, pad, offs, alpha, beta))
     assert sg.get_device_errors() == 0

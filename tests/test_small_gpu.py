@@ -16,7 +16,7 @@ import pytest
 import oracle
 import sgblas_b200 as sg
 from tests import cases as C
-from tests.gpu_util import check_full, run_sgemm, to_device
+from tests.gpu_util import check_full, check_guards, run_sgemm, to_device
 
 pytestmark = pytest.mark.gpu
 
@@ -133,6 +133,7 @@ def test_small_no_alloc(cuda, handle):
                                            pc, case.ldc)
         torch.cuda.synchronize()
         assert status == 0
+        check_guards(da, db, dc)
         _assert(check_full(case, a, b, c, dc.cpu().numpy()), (m, n, k))
     assert sg.get_device_errors() == 0
 

@@ -21,7 +21,7 @@ import pytest
 import oracle
 import sgblas_b200 as sg
 from tests import cases as C
-from tests.gpu_util import c_view, run_sgemm, to_device
+from tests.gpu_util import c_view, check_guards, run_sgemm, to_device
 
 pytestmark = pytest.mark.gpu
 
@@ -141,6 +141,7 @@ def test_tf32_no_alloc_and_batched(cuda, tf32_handle):
                                    ctypes.byref(f(0.0)), pc, case.ldc)
     torch.cuda.synchronize()
     assert st == 0
+    check_guards(da, db, dc)
     check_tf32(case, a, b, c, dc.cpu().numpy(), "noalloc")
     dc2, pc2 = to_device(torch, np.concatenate([c, c]))
     tf32_handle.sgemm_strided_batched(0, 1, case.m, case.n, case.k, 1.0, pa, case.lda, 0, pb,
@@ -153,6 +154,35 @@ def test_tf32_no_alloc_and_batched(cuda, tf32_handle):
         got = both[i * case.c_size:(i + 1) * case.c_size]
         res = oracle.check(c_view(got, case.m, case.n, case.ldc), ref, mag, case.k)
         assert res["ok_north_star"], (i, res)
+
+
+def test_tf32_no_alloc_split_tiles(cuda, tf32_handle):
+    """The TF32 lane through sgblasSgemmNoAlloc on shapes whose schedule
+    splits tiles into k pieces, so the pieces and their arrival counters live
+    in the fixed scratch: two calls in a row (the second reuses the counters
+    the first left), each equal to sgblasSgemm on the same TF32 handle and
+    within the TF32 bound."""
+    torch = cuda
+    f = ctypes.c_float
+    for m, n, k in ((128, 128, 65536), (640, 520, 4100)):
+        case = C.Case("tf32-noalloc-split", 0, 0, m, n, k, m, k, m, 1.0, 0.5)
+        a, b, c = C.cfg_inputs(case, 19, None)
+        status, want = run_sgemm(torch, tf32_handle, case, a, b, c)
+        assert status == 0
+        check_tf32(case, a, b, c, want, "sgemm")
+        da, pa = to_device(torch, a)
+        db, pb = to_device(torch, b)
+        for call in range(2):
+            dc, pc = to_device(torch, c)
+            st = sg.lib.sgblasSgemmNoAlloc(tf32_handle.raw, 0, 0, m, n, k, ctypes.byref(f(1.0)),
+                                           pa, m, pb, k, ctypes.byref(f(0.5)), pc, m)
+            torch.cuda.synchronize()
+            assert st == 0
+            check_guards(da, db, dc)
+            got = dc.cpu().numpy()
+            check_tf32(case, a, b, c, got, f"noalloc call {call}")
+            assert np.array_equal(got, want), (m, n, k, call)
+    assert sg.get_device_errors() == 0
 
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
