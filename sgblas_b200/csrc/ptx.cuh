@@ -24,32 +24,36 @@ constexpr unsigned kErrCounter = 2u;   // an arrival counter could not be update
 
 // ---- split-tile arrival counters --------------------------------------------
 // A tile split into pieces is finished by the CTA whose piece arrives last.
-// Its counter holds (epoch << 32) | arrivals. The host gives every launch
+// Its counter holds (epoch << 32) | arrivals; the host gives every launch
 // that uses a scratch buffer's counters an epoch that no earlier launch on
-// that buffer used, so a counter holding any other epoch -- zero, or what a
-// launch that stopped early (a wait that timed out) left behind -- reads as
-// no arrivals: an interrupted launch cannot make a later one pick the wrong
-// last piece. The last arrival resets its counter to zero, so a CUDA graph
-// that replays one epoch also starts from clean counters.
-constexpr int kCounterCasLimit = 1 << 16;   // far above any tile's piece count
-
-// Counts one arrival of launch `epoch` (non-zero) and returns its number (1
-// for the first piece), or 0 after raising kErrCounter if the update kept
-// failing. Each failed compare-and-swap means another piece arrived, so
-// kCounterCasLimit is never reached in a valid launch.
+// that buffer used. Zero is the clean state: the last arrival resets its
+// counter to zero, so the next launch -- or the next replay of a CUDA graph,
+// which reuses its epoch -- starts clean. A value of another non-zero epoch
+// is what a launch that stopped early (a wait that timed out) left behind:
+// the arrival first swaps it back to zero, so an interrupted launch cannot
+// make a later one pick the wrong last piece.
+//
+// Arrivals use atomicAdd: many pieces of one tile may arrive at once, and a
+// compare-and-swap loop would serialise them into one L2 round trip each. The
+// first arrival stamps the epoch with a second add; arrivals between the two
+// see epoch 0 and count the same way.
+//
+// Returns the arrival's number (1 for the first piece).
 __device__ __forceinline__ unsigned arriveCounter(unsigned long long *counter, unsigned epoch,
                                                   unsigned *err) {
-  unsigned long long seen = 0;
-  for (int i = 0; i < kCounterCasLimit; ++i) {
-    const unsigned long long want = static_cast<unsigned>(seen >> 32) == epoch
-                                        ? seen + 1
-                                        : (static_cast<unsigned long long>(epoch) << 32) | 1ULL;
-    const unsigned long long got = atomicCAS(counter, seen, want);
-    if (got == seen) return static_cast<unsigned>(want & 0xffffffffULL);
-    seen = got;
+  unsigned long long seen;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(seen) : "l"(counter) : "memory");
+  const unsigned seen_epoch = static_cast<unsigned>(seen >> 32);
+  if (seen_epoch != 0 && seen_epoch != epoch) {
+    // Left by an interrupted launch: one of the arrivals that saw it clears
+    // it (the others' swaps fail: the value has moved on).
+    (void)atomicCAS(counter, seen, 0ULL);
   }
-  if (err != nullptr) atomicOr(err, kErrCounter);
-  return 0;
+  const unsigned long long old = atomicAdd(counter, 1ULL);
+  const unsigned old_epoch = static_cast<unsigned>(old >> 32);
+  if (old_epoch != 0 && old_epoch != epoch && err != nullptr) atomicOr(err, kErrCounter);
+  if (old == 0ULL) atomicAdd(counter, static_cast<unsigned long long>(epoch) << 32);
+  return static_cast<unsigned>(old & 0xffffffffULL) + 1U;
 }
 
 __device__ __forceinline__ uint32_t smemAddr(const void *p) {

@@ -36,8 +36,7 @@ sgblasStatus_t launchTiles(kern::GemmParams p, const Scratch &scratch, int devic
   bool used_handle_workspace = false;
   if (s.sk_tiles > 0) {
     const size_t need = kCounterRegionBytes + 2 * static_cast<size_t>(s.grid) * G::kSlotBytes;
-    const bool counters_fit =
-        static_cast<size_t>(s.sk_tiles) * sizeof(Counter) <= kCounterRegionBytes;
+    const bool counters_fit = static_cast<size_t>(s.sk_tiles) <= kMaxCounters;
     unsigned char *base = nullptr;
     if (scratch.fixed != nullptr) {
       // Fixed scratch: refuse rather than allocate. The counters are cleared

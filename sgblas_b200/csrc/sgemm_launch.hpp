@@ -59,14 +59,15 @@ constexpr int kItemCostIters = 3;   // a stream-K part's fix-up and epilogue, in
 Schedule makeSchedule(long long tiles, int kiters, int sms);
 
 // Scratch layout: [arrival counters (kCounterRegionBytes) | partial slots].
-// Counters are 8 bytes (epoch and arrivals, kern::arriveCounter); sk_tiles <=
-// 2 * grid <= 2 * SMs, so 1024 counters cover any GPU with up to 512 SMs. The
-// counter region has a fixed size so that the layout is the same for every
-// call (one launch's counters must never be overlapped by another launch's
-// slots).
+// The counter region holds kMaxCounters 8-byte arrival counters (epoch and
+// count, kern::arriveCounter); sk_tiles <= 2 * grid <= 2 * SMs, so they cover
+// any GPU with up to 512 SMs. The region has a fixed size so that the layout
+// is the same for every call (one launch's counters must never be overlapped
+// by another launch's slots).
 constexpr size_t kSlotBytes = kern::Geo<16>::kSlotBytes;  // the largest slot (128 KiB)
 constexpr size_t kCounterRegionBytes = 8192;
 using Counter = unsigned long long;
+constexpr size_t kMaxCounters = kCounterRegionBytes / sizeof(Counter);   // 1024
 
 // A batch of products sharing sizes, leading dimensions and scalars: matrix
 // i is A + i*stride_a (B, C alike), or a_ptrs[i] etc. when the caller passed

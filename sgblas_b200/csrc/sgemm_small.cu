@@ -531,7 +531,7 @@ sgblasStatus_t launchSmall(bool ta, bool tb, const kern::GemmParams &gp, const S
     const size_t need =
         kCounterRegionBytes + static_cast<size_t>(s.tiles) * p.groups * tile_bytes;
     unsigned char *base = nullptr;
-    if (counters * sizeof(Counter) > kCounterRegionBytes) {
+    if (counters > kMaxCounters) {
       base = nullptr;
     } else if (scratch.fixed != nullptr) {
       if (need <= scratch.fixed_bytes) {

@@ -38,7 +38,7 @@ Schedule scheduleTf32(t::Tf32Params &q, long long tiles, int slots, int units,
   if (s.sk_tiles > 0) {
     const size_t need = kCounterRegionBytes + static_cast<size_t>(slots) * kSlotBytes;
     const size_t counters = static_cast<size_t>(s.sk_tiles) * counters_per_tile;
-    const bool counters_fit = counters * sizeof(Counter) <= kCounterRegionBytes;
+    const bool counters_fit = counters <= kMaxCounters;
     unsigned char *base = nullptr;
     if (scratch.fixed != nullptr) {
       if (counters_fit && need <= scratch.fixed_bytes) {
