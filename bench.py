@@ -75,6 +75,10 @@ def parse_args():
                          "reference benchmark's protocol, bench/benchmark.cu:290-307); the R "
                          "calls are captured once in a CUDA graph and replayed, for ours and "
                          "for cuBLAS alike, so that no host overhead sits between them")
+    ap.add_argument("--rotate", action="store_true",
+                    help="N=1: cold-cache lane of the reference's protocol (docs/benchmarking.md:82): "
+                         "cycle through copies of A, B, C whose total exceeds twice the L2, no "
+                         "flush; cuBLAS gets the same rotation")
     ap.add_argument("--no-sharded-n1", action="store_true",
                     help="N=1: skip the config-5 (32768 x 32768 x 8192) single-GPU line")
     ap.add_argument("--no-e2e", action="store_true")
@@ -431,11 +435,25 @@ def run_single(args) -> None:
         h.set_math_mode(sg.SGBLAS_MATH_TF32)
         plain = False
 
+    # --rotate: workspace sets (A, B, C) used in turn, step by step.
+    rot = []
+    if args.rotate:
+        l2 = getattr(props, "L2_cache_size", 126 << 20)
+        set_bytes = 4 * (da.numel() + db.numel() + dc.numel())
+        count = min(64, max(2, -(-2 * l2 // set_bytes)))
+        rot = [(da, db, dc)] + [(da.clone(), db.clone(), dc.clone()) for _ in range(count - 1)]
+        args.no_flush = True
+    cur = [0]
+
+    def operands():
+        return rot[cur[0] % len(rot)] if rot else (da, db, dc)
+
     def launch():
+        a_, b_, c_ = operands()
         if batch == 1:
-            h.sgemm(ta, tb, m, n, k, alpha, da, lda, db, ldb, beta, dc, ldc)
+            h.sgemm(ta, tb, m, n, k, alpha, a_, lda, b_, ldb, beta, c_, ldc)
         else:
-            h.sgemm_strided_batched(ta, tb, m, n, k, alpha, da, lda, sa, db, ldb, sb, beta, dc,
+            h.sgemm_strided_batched(ta, tb, m, n, k, alpha, a_, lda, sa, b_, ldb, sb, beta, c_,
                                     ldc, sc, batch)
 
     reps = max(1, args.back_to_back)
@@ -447,7 +465,8 @@ def run_single(args) -> None:
             flush.zero_()
 
     with torch.cuda.stream(stream):
-        for _ in range(warmup):
+        for i in range(warmup):
+            cur[0] = i
             flush_l2()
             launch()
     torch.cuda.synchronize()
@@ -469,6 +488,7 @@ def run_single(args) -> None:
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             for i in range(steps):
+                cur[0] = i
                 flush_l2()
                 ev[i][0].record(stream)
                 if graph is not None:
@@ -525,7 +545,10 @@ def run_single(args) -> None:
                                    if plain and (m, n, k, beta) == (4096, 4096, 4096, 0.0) else ""),
                       "m": m, "n": n, "k": k, "lda": lda, "ldb": ldb, "ldc": ldc,
                       "inputs": "uniform[-1,1) float32 (numpy seeds 1: A,B; 2: C)",
-                      "l2": ("not flushed: back-to-back calls" if args.no_flush else
+                      "l2": (f"rotated over {len(rot)} copies of A, B, C "
+                             f"({len(rot) * 4 * (da.numel() + db.numel() + dc.numel()) >> 20} MiB, "
+                             "over twice the L2), no flush" if rot else
+                             "not flushed: back-to-back calls" if args.no_flush else
                              "flushed before every timed step (256 MiB write outside the "
                              "step's CUDA events)")},
            "calls_per_event_pair": reps,
@@ -538,17 +561,22 @@ def run_single(args) -> None:
         try:
             cb = Cublas(tf32=tf32)
             cb.set_stream(stream)
-            dc2 = dc.clone()
+            # cuBLAS writes its own copies of C (ours are checked afterwards)
+            c2 = [x[2].clone() for x in rot] if rot else [dc.clone()]
+
             def cublas_call():
+                a_, b_, _ = operands()
+                c_ = c2[cur[0] % len(c2)]
                 if batch == 1:
-                    return cb.sgemm(ta, tb, m, n, k, alpha, da.data_ptr(), lda, db.data_ptr(),
-                                    ldb, beta, dc2.data_ptr(), ldc)
-                return cb.sgemm_strided_batched(ta, tb, m, n, k, alpha, da.data_ptr(), lda, sa,
-                                                db.data_ptr(), ldb, sb, beta, dc2.data_ptr(), ldc,
+                    return cb.sgemm(ta, tb, m, n, k, alpha, a_.data_ptr(), lda, b_.data_ptr(),
+                                    ldb, beta, c_.data_ptr(), ldc)
+                return cb.sgemm_strided_batched(ta, tb, m, n, k, alpha, a_.data_ptr(), lda, sa,
+                                                b_.data_ptr(), ldb, sb, beta, c_.data_ptr(), ldc,
                                                 sc, batch)
 
             with torch.cuda.stream(stream):
-                for _ in range(warmup):
+                for i in range(warmup):
+                    cur[0] = i
                     st = cublas_call()
             torch.cuda.synchronize()
             assert st == 0
@@ -557,6 +585,7 @@ def run_single(args) -> None:
                    for _ in range(steps)]
             with torch.cuda.stream(stream):
                 for i in range(steps):
+                    cur[0] = i
                     flush_l2()
                     cev[i][0].record(stream)
                     if cgraph is not None:
@@ -573,7 +602,7 @@ def run_single(args) -> None:
                         (" CUDA_R_32F x3, CUBLAS_COMPUTE_32F_FAST_TF32, CUBLAS_TF32_TENSOR_OP_MATH"
                          if tf32 else " CUDA_R_32F x3, CUBLAS_COMPUTE_32F_PEDANTIC, "
                                       "CUBLAS_PEDANTIC_MATH, NVIDIA_TF32_OVERRIDE=0")}
-            del dc2
+            del c2
         except (OSError, AssertionError) as e:
             out["cublas_pedantic"] = {"unavailable": str(e)}
 

@@ -229,6 +229,36 @@ bool capturing(cudaStream_t stream) {
 
 }  // namespace
 
+namespace {
+
+// The handle moved to another device: its workspace is freed on the device
+// it lives on, stream-ordered after its last user there (the legacy stream
+// of that device waits for the workspace event), so that the call does not
+// block the host. False if that cannot be enqueued.
+bool retireOnOwnDevice(sgblasContext *ctx) {
+  int current = -1;
+  if (cudaGetDevice(&current) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  const auto ev = static_cast<cudaEvent_t>(ctx->workspace_event);
+  const bool ok = cudaSetDevice(ctx->workspace_device) == cudaSuccess &&
+                  (ev == nullptr || cudaStreamWaitEvent(cudaStreamLegacy, ev, 0) == cudaSuccess) &&
+                  cudaFreeAsync(ctx->workspace, cudaStreamLegacy) == cudaSuccess;
+  if (ok) {
+    if (ev != nullptr) (void)cudaEventDestroy(ev);   // released once it completes
+    ctx->workspace = nullptr;
+    ctx->workspace_bytes = 0;
+    ctx->workspace_device = -1;
+    ctx->workspace_event = nullptr;
+  }
+  (void)cudaGetLastError();
+  (void)cudaSetDevice(current);
+  return ok;
+}
+
+}  // namespace
+
 bool ensureWorkspace(sgblasContext *ctx, size_t need, int device, cudaStream_t stream) {
   const bool in_capture = capturing(stream);
   if (ctx->workspace != nullptr && ctx->workspace_device == device &&
@@ -257,7 +287,7 @@ bool ensureWorkspace(sgblasContext *ctx, size_t need, int device, cudaStream_t s
       ctx->workspace_device = -1;
       ctx->workspace_event = nullptr;
     }
-  } else {
+  } else if (ctx->workspace != nullptr && !retireOnOwnDevice(ctx)) {
     releaseWorkspace(ctx);
   }
   if (cudaSetDevice(device) != cudaSuccess) {

@@ -340,6 +340,27 @@ def test_split_products_exact_after_interrupted_launch(cuda, handle):
     assert sg.get_device_errors() == 0
 
 
+def test_handle_moves_between_devices(cuda, handle):
+    """One handle used on device 0, 1, 0, 1 in turn with a product that needs
+    the workspace: each move frees the old workspace on its own device,
+    stream-ordered (no host synchronization), and allocates a new one; every
+    result matches the oracle. Needs 2 GPUs."""
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    case = C.Case("move", 0, 0, 1500, 1300, 3000, 1500, 3000, 1500, 1.0, 0.0)
+    a, b, c = C.cfg_inputs(case, 71, None)
+    try:
+        for dev in (0, 1, 0, 1):
+            torch.cuda.set_device(dev)
+            status, out = run_sgemm(torch, handle, case, a, b, c)
+            assert status == 0, dev
+            _assert(check_sampled(case, a, b, c, out, count=4096, seed=dev), ("device", dev))
+            assert sg.get_device_errors() == 0
+    finally:
+        torch.cuda.set_device(0)
+
+
 def test_matches_reference_golden_outputs(cuda, handle):
     """Our outputs at the entries the reference library produced on a B200
     (tests/golden/reference_suite.npz): both lie within the north-star bound
