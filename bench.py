@@ -104,7 +104,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.idx)],
+                 "-lms", "50", "-i", str(self.idx)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -157,6 +157,48 @@ def smi_index(torch, dev: int) -> str:
     if vis:
         return vis.split(",")[dev]
     return str(dev)
+
+
+class NearGpu:
+    """Binds this thread to the CPUs of the NUMA node the GPU hangs off
+    (sysfs local_cpulist) while pinned host buffers are allocated and first
+    touched, so that the kernel places them next to the GPU's PCIe link; the
+    previous affinity is restored on exit. A no-op where the node is unknown."""
+
+    def __init__(self, torch, dev: int):
+        self.cpus = None
+        props = torch.cuda.get_device_properties(dev)
+        ids = [getattr(props, f, None) for f in ("pci_domain_id", "pci_bus_id", "pci_device_id")]
+        if None in ids or not hasattr(os, "sched_setaffinity"):
+            return
+        try:
+            text = open(f"/sys/bus/pci/devices/{ids[0]:04x}:{ids[1]:02x}:{ids[2]:02x}.0/"
+                        "local_cpulist").read().strip()
+        except OSError:
+            return
+        cpus = set()
+        for part in text.split(","):
+            if "-" in part:
+                lo, hi = part.split("-")
+                cpus.update(range(int(lo), int(hi) + 1))
+            elif part:
+                cpus.add(int(part))
+        self.cpus = cpus & os.sched_getaffinity(0) or None
+        self.text = text
+
+    def __enter__(self):
+        self.saved = os.sched_getaffinity(0) if self.cpus else None
+        if self.cpus:
+            os.sched_setaffinity(0, self.cpus)
+        return self
+
+    def __exit__(self, *exc):
+        if self.saved:
+            os.sched_setaffinity(0, self.saved)
+
+    def describe(self) -> str:
+        return (f"pinned host buffers allocated from the GPU's NUMA node (CPUs {self.text})"
+                if self.cpus else "pinned host buffers allocated without NUMA binding")
 
 
 # ---------------------------------------------------------------------------
@@ -623,10 +665,12 @@ def e2e_single(torch, sg, ha, hb, hc, beta, m, n, k, steps, warmup) -> dict:
     A and B (and C when beta != 0) from pinned host memory, runs sgblasSgemm
     and copies C back. Two device buffer sets; copies of step i+1 overlap the
     SGEMM of step i."""
-    pa = torch.from_numpy(ha).pin_memory()
-    pb = torch.from_numpy(hb).pin_memory()
-    pc_in = torch.from_numpy(hc).pin_memory() if beta != 0.0 else None
-    pc = torch.empty(m * n, dtype=torch.float32).pin_memory()
+    near = NearGpu(torch, torch.cuda.current_device())
+    with near:
+        pa = torch.from_numpy(ha).pin_memory()
+        pb = torch.from_numpy(hb).pin_memory()
+        pc_in = torch.from_numpy(hc).pin_memory() if beta != 0.0 else None
+        pc = torch.empty(m * n, dtype=torch.float32).pin_memory()
     sets = [(torch.empty(m * k, device="cuda"), torch.empty(k * n, device="cuda"),
              torch.empty(m * n, device="cuda")) for _ in range(2)]
     s_in, s_comp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
@@ -672,7 +716,8 @@ def e2e_single(torch, sg, ha, hb, hc, beta, m, n, k, steps, warmup) -> dict:
     return {"value": 2.0 * m * n * k * steps / secs / 1e12, "unit": UNIT,
             "h2d_bytes_per_step": 4 * (m * k + k * n + (m * n if pc_in is not None else 0)),
             "d2h_bytes_per_step": 4 * m * n,
-            "steps": steps, "pipelining": "2 buffer sets; H2D, SGEMM and D2H on 3 streams"}
+            "steps": steps, "pipelining": "2 buffer sets; H2D, SGEMM and D2H on 3 streams",
+            "host_memory": near.describe()}
 
 
 # ---------------------------------------------------------------------------
@@ -797,9 +842,11 @@ def e2e_sharded(torch, dist, sg, mg, rank, M, n_loc, K, flops, steps) -> dict:
     """Config 5 through the C ABI from host memory: every step rank 0 copies
     A in, every rank copies its B shard in, runs sgblasMgSgemm and copies its
     C shard out. Two buffer sets overlap the copies of step i+1 with step i."""
-    pa = torch.empty(M * K).uniform_(-1.0, 1.0).pin_memory() if rank == 0 else None
-    pb = torch.empty(K * n_loc).uniform_(-1.0, 1.0).pin_memory()
-    pc = torch.empty(M * n_loc).pin_memory()
+    near = NearGpu(torch, torch.cuda.current_device())
+    with near:
+        pa = torch.empty(M * K).uniform_(-1.0, 1.0).pin_memory() if rank == 0 else None
+        pb = torch.empty(K * n_loc).uniform_(-1.0, 1.0).pin_memory()
+        pc = torch.empty(M * n_loc).pin_memory()
     sets = [(torch.empty(M * K, device="cuda") if rank == 0 else None,
              torch.empty(K * n_loc, device="cuda"), torch.empty(M * n_loc, device="cuda"))
             for _ in range(2)]
@@ -845,7 +892,8 @@ def e2e_sharded(torch, dist, sg, mg, rank, M, n_loc, K, flops, steps) -> dict:
             "h2d_bytes_per_step": 4 * (M * K + K * 32768), "d2h_bytes_per_step": 4 * M * 32768,
             "steps": steps,
             "pipelining": "2 buffer sets per rank; H2D, broadcast+SGEMM and D2H on 3 streams; "
-                          "bytes are whole-job totals (A once on rank 0, B and C over all ranks)"}
+                          "bytes are whole-job totals (A once on rank 0, B and C over all ranks)",
+            "host_memory": near.describe()}
 
 
 _RESULT_FD = None
