@@ -240,6 +240,10 @@ MG_CASES = [
     ("panels-tf32", 0, 0, 4096, 512, 2048, 0, 0, 0, 1.0, 0.0, 1, "tf32", True),
     ("bad-ldb-rank1", 0, 0, 4096, 512, 2048, 0, 0, 0, 1.0, 0.0, 0, "fp32", False),
     ("after-error", 0, 0, 4096, 512, 2048, 0, 0, 0, 0.5, 2.0, 0, "fp32", True),
+    # every column on rank 0: rank 1 only passes A on (n_local = 0)
+    ("all-on-0", 0, 0, 4096, 300, 2048, 0, 0, 0, 1.0, 0.0, 1, "fp32", True),
+    # alpha = 0: nothing is sent, each rank scales its block of C
+    ("scale-only", 0, 0, 1000, 600, 500, 0, 0, 2, 0.0, 0.5, 0, "fp32", False),
 ]
 
 
@@ -259,6 +263,8 @@ def _scenario_products(rank, world, h, stream):
         b = rng.uniform(ldb * (k if tb else n))
         c = rng.uniform(ldc * n)
         first, cols = shard_columns(n, world, rank)
+        if name == "all-on-0":
+            first, cols = (0, n) if rank == 0 else (n, 0)
         if tb:   # op(B) columns are rows of the stored n x k matrix
             b_loc = np.ascontiguousarray(b.reshape(k, ldb)[:, first:first + cols]).ravel()
             ldb_loc = max(cols, 1)
@@ -272,6 +278,8 @@ def _scenario_products(rank, world, h, stream):
             da = torch.full((a.size,), float("nan"), device="cuda")
         else:
             da = None
+        if cols == 0:   # no block of its own: any valid pointers (never read)
+            b_loc = c_loc = np.zeros(1, np.float32)
         db, dc = torch.from_numpy(b_loc).cuda(), torch.from_numpy(c_loc).cuda()
         if name == "bad-ldb-rank1" and rank == 1:
             ldb_loc = 0   # invalid on this rank only
@@ -281,7 +289,13 @@ def _scenario_products(rank, world, h, stream):
                                     dc, ldc)
         torch.cuda.synchronize()
         res = {"case": name, "status": status}
-        if status == 0:
+        if status == 0 and cols == 0:
+            res.update(ok=True, padding_ok=True)
+            if da is not None and rank != root:
+                rows_used = k if ta else m
+                got_a = da.cpu().numpy().reshape(-1, lda)[:, :rows_used]
+                res["a_delivered"] = bool(np.array_equal(got_a, a.reshape(-1, lda)[:, :rows_used]))
+        elif status == 0:
             got = dc.cpu().numpy().reshape(cols, ldc).T[:m, :].astype(np.float64)
             ref, mag = oracle.sgemm_f64(ta, tb, m, n, k, alpha, a, lda, b, ldb, beta, c, ldc,
                                         cols=(first, first + cols))
