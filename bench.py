@@ -651,7 +651,9 @@ def run_single(args) -> None:
     if plain and beta == 0.0:
         out["parity"] = sampled_parity(torch, da, db, dc, m, n, k, lda, ldb, ldc)
     if not args.no_e2e and plain:
-        out["e2e"] = e2e_single(torch, sg, ha, hb, hc, beta, m, n, k, max(10, steps // 4), warmup)
+        # At least 40 steps, so that the first upload and the last download,
+        # which nothing overlaps, weigh little in the steady-state rate.
+        out["e2e"] = e2e_single(torch, sg, ha, hb, hc, beta, m, n, k, max(40, steps // 4), warmup)
     if not args.no_sharded_n1 and plain and (m, n, k, beta) == (4096, 4096, 4096, 0.0):
         out["sharded_n1"] = sharded_n1(torch, sg, 3, 3)
     if not args.no_cpu_baseline and plain:
