@@ -79,6 +79,8 @@ def parse_args():
                     help="N=1: cold-cache lane of the reference's protocol (docs/benchmarking.md:82): "
                          "cycle through copies of A, B, C whose total exceeds twice the L2, no "
                          "flush; cuBLAS gets the same rotation")
+    ap.add_argument("--no-allgather", action="store_true",
+                    help="N>1: skip the lane that also gathers C on every rank each step")
     ap.add_argument("--no-sharded-n1", action="store_true",
                     help="N=1: skip the config-5 (32768 x 32768 x 8192) single-GPU line")
     ap.add_argument("--no-e2e", action="store_true")
@@ -799,6 +801,43 @@ def run_sharded(args) -> None:
               "max_ratio": max(x["max_ratio"] for x in parities),
               "ok": all(x["ok"] for x in parities),
               "method": "every rank: " + mine["method"] + "; A delivered by a further call"}
+    # With the C all-gather: every step also assembles the whole C (ldc == M,
+    # equal column blocks) on every rank with sgblasMgAllGather, after the
+    # product; same timing rules.
+    gathered = None
+    if N % world == 0 and not args.no_allgather:
+        full = torch.empty(M * N, device="cuda")
+        a_only = a if rank == 0 else None
+
+        def step_gather():
+            mg.sgemm(0, 0, M, n_loc, K, 1.0, a_only, M, 0, b, K, 0.0, c, M)
+            mg.all_gather(c, full, M * n_loc)
+
+        with torch.cuda.stream(stream):
+            step_gather()
+        torch.cuda.synchronize()
+        dist.barrier()
+        gev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(steps)]
+        with torch.cuda.stream(stream):
+            for i in range(steps):
+                gev[i][0].record(stream)
+                step_gather()
+                gev[i][1].record(stream)
+        torch.cuda.synchronize()
+        gt = torch.tensor([sum(s_.elapsed_time(e_) for s_, e_ in gev) / 1e3], dtype=torch.float64)
+        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+        # the gathered C against this rank's block of it
+        blk = full.view(N, M)[rank * n_loc:(rank + 1) * n_loc]
+        same = bool(torch.equal(blk, c.view(n_loc, M)))
+        flags = torch.tensor([1 if same else 0], dtype=torch.int64)
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+        gathered = {"value": flops * steps / float(gt.item()) / 1e12, "unit": UNIT,
+                    "ms_per_step": 1e3 * float(gt.item()) / steps, "steps": steps,
+                    "blocks_match": bool(flags.item()),
+                    "what": "each step: the sharded product, then sgblasMgAllGather of C "
+                            f"({4 * M * N >> 20} MiB assembled on every rank); max over ranks"}
+        del full
     del a, b, c, a_full
     torch.cuda.empty_cache()
 
@@ -826,6 +865,7 @@ def run_sharded(args) -> None:
                                        "panels (512, 1024, 2048, ~4096 rows), each rank "
                                        "computing a panel's rows as it arrives"},
                "parity": parity,
+               "with_allgather": gathered,
                "roofline": {"bound": "fp32_fma", "achieved": value, "peak": peak, "unit": UNIT,
                             "frac": value / peak, "traffic": None,
                             "peak_source": f"{world} x {sms} SMs x 128 lanes x 2 x {mhz:.0f} MHz "
