@@ -45,31 +45,42 @@ __global__ __launch_bounds__(kPackThreads) void packColumnsKernel(const float *_
   (void)cols_k;
 }
 
-// k-contiguous source: element (x, k) at src[k + x * ld]. 32 x 32 tiles
-// through shared memory: warps read 32 consecutive k of one x and write 32
-// consecutive x of one k; the padded row makes both shared accesses
-// conflict-free.
+// k-contiguous source: element (x, k) at src[k + x * ld]. Tiles of 32 x by
+// 64 k through shared memory: warps read 32 consecutive k of one x (eight
+// independent loads per thread, issued together) and write 32 consecutive x
+// of one k; the padded row makes both shared accesses conflict-free.
 constexpr int kTile = 32;
+constexpr int kTileK = 64;
 __global__ __launch_bounds__(kPackThreads) void packTransposeKernel(const float *__restrict__ src,
                                                                    int ld, int rows_x, int cols_k,
                                                                    float *__restrict__ dst,
                                                                    int ldp, int tiles_x,
                                                                    long long tiles) {
-  __shared__ float tile[kTile][kTile + 1];
+  __shared__ float tile[kTile][kTileK + 1];
   const int lane = threadIdx.x % 32, row = threadIdx.x / 32;
+  constexpr int kRowsPerPass = kPackThreads / 32;
   kern::gridDependencyWait();
   kern::allowDependentLaunch();
   for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int x0 = static_cast<int>(t % tiles_x) * kTile;
-    const int k0 = static_cast<int>(t / tiles_x) * kTile;
+    const int k0 = static_cast<int>(t / tiles_x) * kTileK;
+    float v[kTile / kRowsPerPass][2];
 #pragma unroll
-    for (int r = row; r < kTile; r += kPackThreads / 32) {
-      const int x = x0 + r, k = k0 + lane;
-      tile[r][lane] = (x < rows_x && k < cols_k) ? src[static_cast<size_t>(x) * ld + k] : 0.0F;
+    for (int i = 0; i < kTile / kRowsPerPass; ++i) {
+      const int x = x0 + row + i * kRowsPerPass;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int k = k0 + lane + 32 * h;
+        v[i][h] = (x < rows_x && k < cols_k) ? src[static_cast<size_t>(x) * ld + k] : 0.0F;
+      }
     }
+#pragma unroll
+    for (int i = 0; i < kTile / kRowsPerPass; ++i)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) tile[row + i * kRowsPerPass][lane + 32 * h] = v[i][h];
     __syncthreads();
 #pragma unroll
-    for (int r = row; r < kTile; r += kPackThreads / 32) {
+    for (int r = row; r < kTileK; r += kRowsPerPass) {
       const int k = k0 + r, x = x0 + lane;
       if (k < cols_k && x < rows_x) dst[static_cast<size_t>(k) * ldp + x] = tile[lane][r];
     }
@@ -86,7 +97,7 @@ sgblasStatus_t launchPack(const float *src, int ld, bool k_contiguous, int rows_
   const void *kernel;
   if (k_contiguous) {
     tiles_x = (rows_x + kTile - 1) / kTile;
-    tiles = static_cast<long long>(tiles_x) * ((cols_k + kTile - 1) / kTile);
+    tiles = static_cast<long long>(tiles_x) * ((cols_k + kTileK - 1) / kTileK);
     kernel = reinterpret_cast<const void *>(packTransposeKernel);
   } else {
     tiles_x = (rows_x + 4 * kPackThreads - 1) / (4 * kPackThreads);

@@ -458,13 +458,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     auto wait = [&](uint64_t *bar, int parity) {
       if (ok) ok = mbarWait(bar, static_cast<uint32_t>(parity), p.err);
     };
-    // With beta != 0 the epilogue of a whole tile reads its block of C. The
-    // producer prefetches that block into L2 when it starts loading the tile,
-    // a whole tile's main loop before the read: one column per thread, the
-    // 16-byte aligned interior of the in-range rows (never outside C).
+    // With beta != 0 the epilogue of a tile reads its block of C. The
+    // producer prefetches that block into L2 when it starts loading the item
+    // that will most likely run that epilogue, a whole main loop before the
+    // read: a whole tile, or the first piece (k from 0) of a split tile --
+    // the CTA owning it reaches that piece at the end of its range, after
+    // the owners of the later pieces have started theirs, so it is the last
+    // to arrive. One column per thread, the 16-byte aligned interior of the
+    // in-range rows (never outside C).
     auto prefetchC = [&](const Item &it, int tm0, int tn0, int bi) {
       if constexpr (kBeta != Beta::kZero) {
-        if (it.kb != 0 || it.ke != p.kiters) return;
+        if (it.kb != 0) return;
         const int r1 = min(tm0 + P::kBM, p.m);
         const float *cbase = matrixC(bi);
 #pragma unroll 1

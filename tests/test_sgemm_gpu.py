@@ -249,6 +249,25 @@ def test_stream_k_shapes(cuda, handle, m, n, k, ta, tb):
         _assert(check_sampled(case, a, b, c, out), (m, n, k))
 
 
+# Thin edge tiles under stream-K: n % 128 of 1, 20, 64 and 65 leave a last
+# tile column that is mostly outside C; m % 128 == 1 puts the thin edge on the
+# other side of C. Operands are copied (ld % 4 != 0) or read in place.
+THIN_SHAPES = [(896, 2049, 333), (1000, 1300, 2000), (1024, 1088, 640), (640, 1089, 1500),
+               (1025, 1024, 900)]
+
+
+@pytest.mark.parametrize("m,n,k", THIN_SHAPES)
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 1)])
+def test_thin_edge_tiles(cuda, handle, m, n, k, ta, tb):
+    lda = (k if ta else m) + 3
+    ldb = (n if tb else k) + 4
+    case = C.Case("thin", ta, tb, m, n, k, lda, ldb, m + 1, 1.5, -0.5)
+    a, b, c = C.cfg_inputs(case, m + 2 * n + k, None, normal=True)
+    status, out = run_sgemm(cuda, handle, case, a, b, c)
+    assert status == 0
+    _assert(check_full(case, a, b, c, out), (m, n, k, ta, tb))
+
+
 def test_workspace_shared_across_streams(cuda, handle):
     """One handle alternating between two streams with no host sync between
     calls: the workspace is ordered by an event, results are bit-identical to
