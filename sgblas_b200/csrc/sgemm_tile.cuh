@@ -671,71 +671,65 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       }
   };
 
-  int c_idx = 0;
-  int c_kt, c_ke;
-  {
-    const Item it = itemAt(p, cta, 0);
-    c_kt = it.kb;
-    c_ke = it.ke;
-  }
-  for (int g = 0; g < total; ++g) {
-    const int s = g % kStages;
-    const int t = g % kTransBufs;
-    // With a transposed operand, tfull[t] implies full[s]: every producer
-    // thread waited for stage s to land before transposing it and arriving
-    // on tfull[t] (release), so acquiring tfull[t] also makes the stage's TMA
-    // or cp.async data visible. One wait per iteration instead of two.
-    if constexpr (P::kTrans) wait(&tfull[t], (g / kTransBufs) & 1);
-    else wait(&full[s], (g / kStages) & 1);
-    computeStage<kTP>(P::kTransP ? tbufP(t) : stageP(s), P::kTransD ? tbufD(t) : stageD(s),
-                      p_base, d_base, acc);
-    __syncwarp();
-    if (lane == 0) {
-      mbarArrive(&empty[s]);
-      if constexpr (P::kTrans) mbarArrive(&tempty[t]);
+  // One item at a time: its k iterations in a tight loop, then its epilogue.
+  // g counts iterations over all items (stage g % kStages, transposed buffer
+  // g % kTransBufs).
+  int g = 0;
+  for (int c_idx = 0; c_idx < nitems; ++c_idx) {
+    const Item c_item = itemAt(p, cta, c_idx);
+    const int g_end = g + (c_item.ke - c_item.kb);
+#pragma unroll 1
+    for (; g < g_end; ++g) {
+      const int s = g % kStages;
+      const int t = g % kTransBufs;
+      // With a transposed operand, tfull[t] implies full[s]: every producer
+      // thread waited for stage s to land before transposing it and arriving
+      // on tfull[t] (release), so acquiring tfull[t] also makes the stage's
+      // TMA or cp.async data visible. One wait per iteration instead of two.
+      if constexpr (P::kTrans) wait(&tfull[t], (g / kTransBufs) & 1);
+      else wait(&full[s], (g / kStages) & 1);
+      computeStage<kTP>(P::kTransP ? tbufP(t) : stageP(s), P::kTransD ? tbufD(t) : stageD(s),
+                        p_base, d_base, acc);
+      __syncwarp();
+      if (lane == 0) {
+        mbarArrive(&empty[s]);
+        if constexpr (P::kTrans) mbarArrive(&tempty[t]);
+      }
     }
 
-    if (++c_kt == c_ke) {
-      const Item c_item = itemAt(p, cta, c_idx);
-      int c_m0, c_n0, c_bi;
-      origin(c_item.tile, &c_m0, &c_n0, &c_bi);
-      if (c_item.kb == 0 && c_item.ke == p.kiters) {
-        storeTile(c_m0, c_n0, c_bi);
-      } else {
-        // Stream-K piece: publish, count the arrival, and let the last
-        // arriving piece reduce all pieces in piece order.
-        const int u = c_item.tile - p.dp_tiles;
-        const int first = skOwner(p, u * p.kiters);
-        const int last = skOwner(p, (u + 1) * p.kiters - 1);
-        publish(skSlot(p, cta, u));
+    int c_m0, c_n0, c_bi;
+    origin(c_item.tile, &c_m0, &c_n0, &c_bi);
+    if (c_item.kb == 0 && c_item.ke == p.kiters) {
+      storeTile(c_m0, c_n0, c_bi);
+    } else {
+      // Stream-K piece: publish, count the arrival, and let the last
+      // arriving piece reduce all pieces in piece order.
+      const int u = c_item.tile - p.dp_tiles;
+      const int first = skOwner(p, u * p.kiters);
+      const int last = skOwner(p, (u + 1) * p.kiters - 1);
+      publish(skSlot(p, cta, u));
+      __threadfence();
+      namedBarrier<1, kThreads>();
+      if (tid == 0)
+        last_arrival = arriveCounter(p.counters + u, p.epoch, p.err) ==
+                       static_cast<unsigned>(last - first + 1);
+      namedBarrier<1, kThreads>();
+      if (last_arrival) {
         __threadfence();
-        namedBarrier<1, kThreads>();
-        if (tid == 0)
-          last_arrival = arriveCounter(p.counters + u, p.epoch, p.err) ==
-                         static_cast<unsigned>(last - first + 1);
-        namedBarrier<1, kThreads>();
-        if (last_arrival) {
-          __threadfence();
 #pragma unroll
-          for (int i = 0; i < kTP / 2; ++i)
+        for (int i = 0; i < kTP / 2; ++i)
 #pragma unroll
-            for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
+          for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
 #pragma unroll 1
-          for (int c = first; c <= last; ++c) gather(skSlot(p, c, u));
-          storeTile(c_m0, c_n0, c_bi);
-          if (tid == 0) p.counters[u] = 0;  // ready for the next launch
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < kTP / 2; ++i)
-#pragma unroll
-        for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
-      if (++c_idx < nitems) {
-        const Item it = itemAt(p, cta, c_idx);
-        c_kt = it.kb;
-        c_ke = it.ke;
+        for (int c = first; c <= last; ++c) gather(skSlot(p, c, u));
+        storeTile(c_m0, c_n0, c_bi);
+        if (tid == 0) p.counters[u] = 0;  // ready for the next launch
       }
     }
+#pragma unroll
+    for (int i = 0; i < kTP / 2; ++i)
+#pragma unroll
+      for (int j = 0; j < kTD; ++j) acc[i][j] = make_float2(0.0F, 0.0F);
   }
 }
 
