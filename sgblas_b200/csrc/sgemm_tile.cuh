@@ -483,60 +483,100 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         }
       }
     };
-    int idx = 0, kt, ke, m0, n0, bi;
-    const float *a_src = nullptr, *b_src = nullptr;  // cp.async: this item's matrices
-    auto startItem = [&](const Item &it) {
-      kt = it.kb;
-      ke = it.ke;
-      origin(it.tile, &m0, &n0, &bi);
-      if constexpr (kSrc == Src::kCopy) {
-        a_src = matrixA(bi);
-        b_src = matrixB(bi);
-      }
-      prefetchC(it, m0, n0, bi);
-    };
-    startItem(itemAt(p, cta, 0));
-    // Transposes trail the loads by kLag iterations: far enough behind for the
-    // data to have landed, early enough to stay up to two iterations ahead of
-    // the compute warps. Deadlock-free: the load of iteration i waits for the
-    // consumers to release iteration i - kStages, and the transpose of
-    // iteration j = i - kLag waits for them to release j - kTransBufs; with
-    // kTransBufs >= kStages - kLag both point at iterations the consumers can
-    // finish without this transpose.
-    constexpr int kLag = P::kTrans ? kStages - 3 : 0;
-    static_assert(!P::kTrans || kTransBufs >= kStages - kLag, "transposed ring too small");
-    for (int i = 0; i < total + kLag; ++i) {
-      if (i < total) {
-        const int s = i % kStages;
-        const int k0 = kt * kBK;
-        if constexpr (kSrc == Src::kTma) {
-          if (pt == 0) {
-            if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
-            mbarArriveExpectTx(&full[s], kStageBytes);
-            if (P::kA == Layout::kXK) tmaLoad3d(stageA(s), &p.tma_a, &full[s], m0, k0, bi);
-            else tmaLoad3d(stageA(s), &p.tma_a, &full[s], k0, m0, bi);
-            if (P::kB == Layout::kXK) tmaLoad3d(stageB(s), &p.tma_b, &full[s], n0, k0, bi);
-            else tmaLoad3d(stageB(s), &p.tma_b, &full[s], k0, n0, bi);
-          }
-        } else {
-          if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
-          copyOperand<P::kAExt, P::kA == Layout::kKX>(a_src, p.lda, p.m, p.k, stageA(s), m0, k0,
-                                                       pt, p.a_vec);
-          copyOperand<P::kBExt, P::kB == Layout::kKX>(b_src, p.ldb, p.n, p.k, stageB(s), n0, k0,
-                                                       pt, p.b_vec);
-          cpAsyncArrive(&full[s]);
+    if constexpr (!P::kTrans) {
+      // No transposes: one item at a time, its loads in a loop of their own
+      // (measured faster than the flat loop below for these plans, slower
+      // for the transposing ones).
+      int i = 0;   // iterations loaded so far, over all items
+      for (int idx = 0; idx < nitems; ++idx) {
+        const Item it = itemAt(p, cta, idx);
+        int m0, n0, bi;
+        origin(it.tile, &m0, &n0, &bi);
+        const float *a_src = nullptr, *b_src = nullptr;  // cp.async: this item's matrices
+        if constexpr (kSrc == Src::kCopy) {
+          a_src = matrixA(bi);
+          b_src = matrixB(bi);
         }
-        if (++kt == ke && ++idx < nitems) startItem(itemAt(p, cta, idx));
+        prefetchC(it, m0, n0, bi);
+#pragma unroll 1
+        for (int kt = it.kb; kt < it.ke; ++kt, ++i) {
+          const int s = i % kStages;
+          const int k0 = kt * kBK;
+          if constexpr (kSrc == Src::kTma) {
+            if (pt == 0) {
+              if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
+              mbarArriveExpectTx(&full[s], kStageBytes);
+              if (P::kA == Layout::kXK) tmaLoad3d(stageA(s), &p.tma_a, &full[s], m0, k0, bi);
+              else tmaLoad3d(stageA(s), &p.tma_a, &full[s], k0, m0, bi);
+              if (P::kB == Layout::kXK) tmaLoad3d(stageB(s), &p.tma_b, &full[s], n0, k0, bi);
+              else tmaLoad3d(stageB(s), &p.tma_b, &full[s], k0, n0, bi);
+            }
+          } else {
+            if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
+            copyOperand<P::kAExt, P::kA == Layout::kKX>(a_src, p.lda, p.m, p.k, stageA(s), m0,
+                                                         k0, pt, p.a_vec);
+            copyOperand<P::kBExt, P::kB == Layout::kKX>(b_src, p.ldb, p.n, p.k, stageB(s), n0,
+                                                         k0, pt, p.b_vec);
+            cpAsyncArrive(&full[s]);
+          }
+        }
       }
-      if constexpr (P::kTrans) {
-        const int j = i - kLag;
-        if (j >= 0) {
-          const int t = j % kTransBufs;
-          wait(&full[j % kStages], (j / kStages) & 1);
-          if (j >= kTransBufs) wait(&tempty[t], (j / kTransBufs - 1) & 1);
-          if constexpr (P::kTransP) transposeKX<kBP>(stageP(j % kStages), tbufP(t), pt);
-          if constexpr (P::kTransD) transposeKX<kBD>(stageD(j % kStages), tbufD(t), pt);
-          mbarArrive(&tfull[t]);
+    } else {
+      int idx = 0, kt, ke, m0, n0, bi;
+      const float *a_src = nullptr, *b_src = nullptr;  // cp.async: this item's matrices
+      auto startItem = [&](const Item &it) {
+        kt = it.kb;
+        ke = it.ke;
+        origin(it.tile, &m0, &n0, &bi);
+        if constexpr (kSrc == Src::kCopy) {
+          a_src = matrixA(bi);
+          b_src = matrixB(bi);
+        }
+        prefetchC(it, m0, n0, bi);
+      };
+      startItem(itemAt(p, cta, 0));
+      // Transposes trail the loads by kLag iterations: far enough behind for the
+      // data to have landed, early enough to stay up to two iterations ahead of
+      // the compute warps. Deadlock-free: the load of iteration i waits for the
+      // consumers to release iteration i - kStages, and the transpose of
+      // iteration j = i - kLag waits for them to release j - kTransBufs; with
+      // kTransBufs >= kStages - kLag both point at iterations the consumers can
+      // finish without this transpose.
+      constexpr int kLag = P::kTrans ? kStages - 3 : 0;
+      static_assert(!P::kTrans || kTransBufs >= kStages - kLag, "transposed ring too small");
+      for (int i = 0; i < total + kLag; ++i) {
+        if (i < total) {
+          const int s = i % kStages;
+          const int k0 = kt * kBK;
+          if constexpr (kSrc == Src::kTma) {
+            if (pt == 0) {
+              if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
+              mbarArriveExpectTx(&full[s], kStageBytes);
+              if (P::kA == Layout::kXK) tmaLoad3d(stageA(s), &p.tma_a, &full[s], m0, k0, bi);
+              else tmaLoad3d(stageA(s), &p.tma_a, &full[s], k0, m0, bi);
+              if (P::kB == Layout::kXK) tmaLoad3d(stageB(s), &p.tma_b, &full[s], n0, k0, bi);
+              else tmaLoad3d(stageB(s), &p.tma_b, &full[s], k0, n0, bi);
+            }
+          } else {
+            if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
+            copyOperand<P::kAExt, P::kA == Layout::kKX>(a_src, p.lda, p.m, p.k, stageA(s), m0, k0,
+                                                         pt, p.a_vec);
+            copyOperand<P::kBExt, P::kB == Layout::kKX>(b_src, p.ldb, p.n, p.k, stageB(s), n0, k0,
+                                                         pt, p.b_vec);
+            cpAsyncArrive(&full[s]);
+          }
+          if (++kt == ke && ++idx < nitems) startItem(itemAt(p, cta, idx));
+        }
+        if constexpr (P::kTrans) {
+          const int j = i - kLag;
+          if (j >= 0) {
+            const int t = j % kTransBufs;
+            wait(&full[j % kStages], (j / kStages) & 1);
+            if (j >= kTransBufs) wait(&tempty[t], (j / kTransBufs - 1) & 1);
+            if constexpr (P::kTransP) transposeKX<kBP>(stageP(j % kStages), tbufP(t), pt);
+            if constexpr (P::kTransD) transposeKX<kBD>(stageD(j % kStages), tbufD(t), pt);
+            mbarArrive(&tfull[t]);
+          }
         }
       }
     }
