@@ -70,6 +70,17 @@ __device__ __forceinline__ void fenceBarrierInit() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Orders this thread's view of shared memory in the generic proxy before
+// its later async-proxy operations. A stage that the compute warps read with
+// ordinary loads and TMA then refills is a write-after-read across proxies:
+// the empty-barrier hand-off orders the reads only in the generic proxy, so
+// the producer issues this fence after acquiring the stage and before the
+// TMA that overwrites it (without it a refill can land while a lagging warp
+// is still reading the previous contents).
+__device__ __forceinline__ void fenceProxyAsyncShared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void mbarArriveExpectTx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smemAddr(bar)),
                "r"(bytes)

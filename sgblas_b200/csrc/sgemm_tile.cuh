@@ -504,7 +504,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           const int k0 = kt * kBK;
           if constexpr (kSrc == Src::kTma) {
             if (pt == 0) {
-              if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
+              if (i >= kStages) {
+                wait(&empty[s], (i / kStages - 1) & 1);
+                fenceProxyAsyncShared();   // the compute warps read stage s with ld.shared
+              }
               mbarArriveExpectTx(&full[s], kStageBytes);
               if (P::kA == Layout::kXK) tmaLoad3d(stageA(s), &p.tma_a, &full[s], m0, k0, bi);
               else tmaLoad3d(stageA(s), &p.tma_a, &full[s], k0, m0, bi);
@@ -550,7 +553,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           const int k0 = kt * kBK;
           if constexpr (kSrc == Src::kTma) {
             if (pt == 0) {
-              if (i >= kStages) wait(&empty[s], (i / kStages - 1) & 1);
+              if (i >= kStages) {
+                wait(&empty[s], (i / kStages - 1) & 1);
+                fenceProxyAsyncShared();   // the compute warps read stage s with ld.shared
+              }
               mbarArriveExpectTx(&full[s], kStageBytes);
               if (P::kA == Layout::kXK) tmaLoad3d(stageA(s), &p.tma_a, &full[s], m0, k0, bi);
               else tmaLoad3d(stageA(s), &p.tma_a, &full[s], k0, m0, bi);

@@ -268,6 +268,42 @@ def test_thin_edge_tiles(cuda, handle, m, n, k, ta, tb):
     _assert(check_full(case, a, b, c, out), (m, n, k, ta, tb))
 
 
+# ---- stage refills behind a slow epilogue ---------------------------------------
+@pytest.mark.parametrize("ta,tb", [(0, 1), (0, 0)])
+@pytest.mark.parametrize("beta", [1.0, 0.5])
+def test_stage_refill_after_slow_epilogue(cuda, handle, ta, tb, beta):
+    """A TMA refill of a pipeline stage must not land while a compute warp still
+    reads the stage's previous contents. 8192 x 8192 x 256 with beta != 0 has 16
+    k-iterations per tile and a 256 MiB C (larger than L2): every tile's epilogue
+    reads C from HBM, the compute warps fall behind the producer and drift apart.
+    Before the cross-proxy fence between the empty-barrier hand-off and the TMA
+    refill, about half of such calls returned one to three tiles with a few
+    k-terms wrong. Three calls each, every entry against an FP64 product on the
+    GPU (a sampled check would miss a single bad tile most of the time)."""
+    torch = cuda
+    m = n = 8192
+    k = 256
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11 + 2 * ta + tb)
+    a = torch.rand(m * k, device="cuda", generator=g) * 2 - 1
+    b = torch.rand(k * n, device="cuda", generator=g) * 2 - 1
+    c = torch.rand(m * n, device="cuda", generator=g) * 2 - 1
+    lda, ldb = (k if ta else m), (n if tb else k)
+    op_a = (a.view(m, k) if ta else a.view(k, m).T).double()
+    op_b = (b.view(k, n) if tb else b.view(n, k).T).double()
+    c0 = c.view(n, m).T.double()
+    ref = op_a @ op_b + beta * c0
+    bound = 2 * k * 2.0 ** -24 * (op_a.abs() @ op_b.abs() + abs(beta) * c0.abs())
+    del op_a, op_b
+    for call in range(3):
+        out = c.clone()
+        handle.sgemm(ta, tb, m, n, k, 1.0, a, lda, b, ldb, beta, out, m)
+        torch.cuda.synchronize()
+        bad = int(((out.view(n, m).T.double() - ref).abs() > bound).sum())
+        assert bad == 0, (ta, tb, beta, call, bad)
+    assert sg.get_device_errors() == 0
+
+
 def test_workspace_shared_across_streams(cuda, handle):
     """One handle alternating between two streams with no host sync between
     calls: the workspace is ordered by an event, results are bit-identical to
