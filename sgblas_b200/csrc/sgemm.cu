@@ -418,9 +418,17 @@ sgblasStatus_t launchProduct(sgblasContext *ctx, sgblasOperation_t ta, sgblasOpe
   // matrix (A: m x k, as for op N; B: n x k, as for op T) with an aligned
   // leading dimension, and the product runs on TMA staging. Without a
   // workspace, and for batches, the tile kernel stages it with cp.async.
+  // In a large FP32 product a k-contiguous operand (A transposed, B not) is
+  // copied the same way so that the kernel needs no transposes, when the
+  // other side of C is at least kPackReuse long (see sgemm_launch.hpp).
   const bool single = batch.count == 1 && batch.a_ptrs == nullptr;
-  const bool pack_a = single && !(aligned16(a) && lda % 4 == 0);
-  const bool pack_b = single && !(aligned16(b) && ldb % 4 == 0);
+  const bool fp32 = ctx->math_mode != SGBLAS_MATH_TF32;
+  auto worthCopy = [&](long long reuse, long long rows_x) {
+    return fp32 && reuse >= kPackReuse &&
+           static_cast<size_t>(rows_x) * static_cast<size_t>(k) * sizeof(float) <= kPackMaxBytes;
+  };
+  const bool pack_a = single && (!(aligned16(a) && lda % 4 == 0) || (tA && worthCopy(n, m)));
+  const bool pack_b = single && (!(aligned16(b) && ldb % 4 == 0) || (!tB && worthCopy(m, n)));
   bool packed = false;
   if (pack_a || pack_b) {
     const int sms = smCount(device);
