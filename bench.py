@@ -81,6 +81,9 @@ def parse_args():
                          "flush; cuBLAS gets the same rotation")
     ap.add_argument("--no-allgather", action="store_true",
                     help="N>1: skip the lane that also gathers C on every rank each step")
+    ap.add_argument("--no-launch-count", action="store_true",
+                    help="report the launch estimate instead of tracing one extra call (for "
+                         "runs under ncu, which owns the profiling interface)")
     ap.add_argument("--no-sharded-n1", action="store_true",
                     help="N=1: skip the config-5 (32768 x 32768 x 8192) single-GPU line")
     ap.add_argument("--no-e2e", action="store_true")
@@ -257,6 +260,23 @@ def profile_traffic(name: str):
         return None
     m = re.search(r"traffic_bytes_per_launch\s*[:=]\s*([0-9.eE+]+)", path.read_text())
     return float(m.group(1)) if m else None
+
+
+def own_launches(torch, fn):
+    """Kernels of this library that fn() launches, counted from the CUDA
+    activity trace of torch.profiler over one extra call outside the timed
+    region (names in the sgblas namespace: the product kernels and the operand
+    copies). Nothing is timed under the profiler. None if it cannot trace."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        return sum(1 for e in prof.events()
+                   if e.device_type == torch.autograd.DeviceType.CUDA and "sgblas" in e.name)
+    except Exception:  # noqa: BLE001  (no CUPTI: the caller reports its own estimate)
+        return None
 
 
 def fp32_peak_tflops(sms: int, mhz: float) -> float:
@@ -547,6 +567,16 @@ def run_single(args) -> None:
     clocks = clk.summary()
     if sg.get_device_errors() != 0:
         raise RuntimeError("device error flags raised during the bench")
+    per_step = None
+    if not args.no_launch_count:
+        with torch.cuda.stream(stream):
+            per_step = own_launches(torch, launch)
+    if per_step is None:
+        launches, launches_method = steps * reps, "estimate: one product kernel per call"
+    else:
+        launches = steps * per_step
+        launches_method = (f"{per_step} sgblas kernel(s) per step, counted on one extra "
+                           "untimed step with the torch.profiler CUDA trace")
 
     mhz = clocks["sm_mhz"] or 1965.0
     peak = fp32_peak_tflops(sms, mhz)
@@ -598,7 +628,8 @@ def run_single(args) -> None:
            "calls_per_event_pair": reps,
            "launch": ("the calls of a step replayed as one CUDA graph" if args.back_to_back
                       else "one call per step from the host"),
-           "roofline": roofline, "clocks": clocks, "gpu_launches": steps * reps,
+           "roofline": roofline, "clocks": clocks, "gpu_launches": launches,
+           "gpu_launches_method": launches_method,
            "device": props.name}
 
     if not args.no_cublas:
@@ -787,6 +818,14 @@ def run_sharded(args) -> None:
     allc = [None] * world
     dist.all_gather_object(allc, clocks)
     errors = sg.get_device_errors()
+    # Launches: one more (untimed) step on every rank under the profiler's
+    # CUDA trace; C is recomputed with the same values.
+    per_step = None
+    if not args.no_launch_count:
+        with torch.cuda.stream(stream):
+            per_step = own_launches(torch, step)
+    counts = [None] * world
+    dist.all_gather_object(counts, per_step)
     # Parity of the timed steps' C (outside the timed region): one more call
     # with no columns of its own delivers A to every rank (C untouched), then
     # each rank checks its shard against FP64.
@@ -872,8 +911,13 @@ def run_sharded(args) -> None:
                                            "(median sampled SM clock)"},
                "clocks": {"sm_mhz": mhz, "sm_max_mhz": max((x["sm_max_mhz"] or 0) for x in allc),
                           "reasons": reasons},
-               "gpu_launches": steps * len(panel_plan(M, K, world)),
-               "gpu_launches_note": "per rank: one product kernel per row panel of A per step",
+               "gpu_launches": (steps * max(counts) if None not in counts
+                                else steps * len(panel_plan(M, K, world))),
+               "gpu_launches_note": ("per rank (the largest count over ranks): sgblas kernels "
+                                     "of one extra untimed step, torch.profiler CUDA trace"
+                                     if None not in counts else
+                                     "estimate per rank: one product kernel per row panel of A "
+                                     "per step"),
                "e2e": e2e}
         emit(json.dumps(out))
     dist.barrier()
