@@ -268,6 +268,23 @@ def test_thin_edge_tiles(cuda, handle, m, n, k, ta, tb):
     _assert(check_full(case, a, b, c, out), (m, n, k, ta, tb))
 
 
+# ---- transpose-free copies of k-contiguous operands --------------------------
+# Both sides of C at least 3072 long: in a large FP32 product a k-contiguous
+# operand that TMA could read in place (A in TN/TT, B in NN/TN) is copied into
+# the workspace first, so that the kernel needs no transposes. Every entry
+# against the oracle, with padded leading dimensions and beta != 0.
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_transpose_free_copies(cuda, handle, ta, tb):
+    m, n, k = 3100, 3072, 700
+    lda = (k if ta else m) + 4
+    ldb = (n if tb else k) + 8
+    case = C.Case("copy-large", ta, tb, m, n, k, lda, ldb, m + 4, 0.75, -0.5)
+    a, b, c = C.cfg_inputs(case, 17 + 2 * ta + tb, None, normal=True)
+    status, out = run_sgemm(cuda, handle, case, a, b, c)
+    assert status == 0
+    _assert(check_full(case, a, b, c, out), (ta, tb))
+
+
 # ---- stage refills behind a slow epilogue ---------------------------------------
 @pytest.mark.parametrize("ta,tb", [(0, 1), (0, 0)])
 @pytest.mark.parametrize("beta", [1.0, 0.5])
