@@ -67,6 +67,10 @@ constexpr int kThreads = 32 * kWarpsP * kWarpsD;   // compute threads (256)
 constexpr int kConsumerWarps = kThreads / 32;
 constexpr int kProducerThreads = 128;               // one warpgroup
 constexpr int kBlockThreads = kThreads + kProducerThreads;
+// With TMA staging and a transposed operand, warp 0 of the producer issues the
+// loads and the other three warps transpose.
+constexpr int kTransposers = kProducerThreads - 32;
+constexpr int kSplitMinIters = 24;
 // Register split: the block is launched with kLaunchRegs per thread (what
 // __launch_bounds__(384, 1) leaves ptxas); setmaxnreg then moves registers
 // from the producer warpgroup to the compute warpgroups.
@@ -273,14 +277,14 @@ __device__ __forceinline__ void copyOperand(const float *src, int ld, int x_limi
 }
 
 // [x][k] tile of kRows rows (64-byte swizzled) -> [k][x] (kRows floats per k),
-// by the producer warpgroup: thread t moves rows t, t+128, ... A warp reads 32
+// by kN producer threads: thread t moves rows t, t + kN, ... A warp reads 32
 // consecutive rows at one chunk -- conflict-free thanks to the swizzle -- and
 // writes 32 consecutive floats per k.
-template <int kRows>
+template <int kRows, int kN = kProducerThreads>
 __device__ __forceinline__ void transposeKX(const float *src, float *dst, int tid) {
-  static_assert(kRows % kProducerThreads == 0 && kBK == 16, "row split");
+  static_assert(kBK == 16, "64-byte rows");
 #pragma unroll
-  for (int r = tid; r < kRows; r += kProducerThreads) {
+  for (int r = tid; r < kRows; r += kN) {
     const char *row = reinterpret_cast<const char *>(src) + r * 64;
     const int phase = (r >> 1) & 3;
     float *d = dst + r;
@@ -425,6 +429,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     total += it.ke - it.kb;
   }
   const int tid = threadIdx.x;
+  // Transposing plans staged by TMA split the producer into a loading warp
+  // and three transposing warps when the CTA has enough iterations (measured:
+  // faster from 1024^3 up, slower for a single short piece, e.g. 768^3).
+  const bool split_producer = P::kTrans && kSrc == Src::kTma && total >= kSplitMinIters;
 
   if (tid == 0) {
     if constexpr (kSrc == Src::kTma) {
@@ -438,7 +446,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     }
 #pragma unroll
     for (int t = 0; t < kTransBufs; ++t) {
-      mbarInit(&tfull[t], kProducerThreads);
+      mbarInit(&tfull[t], split_producer ? kTransposers : kProducerThreads);
       mbarInit(&tempty[t], kConsumerWarps);
     }
     fenceBarrierInit();
@@ -466,13 +474,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     // the owners of the later pieces have started theirs, so it is the last
     // to arrive. One column per thread, the 16-byte aligned interior of the
     // in-range rows (never outside C).
-    auto prefetchC = [&](const Item &it, int tm0, int tn0, int bi) {
+    auto prefetchC = [&](const Item &it, int tm0, int tn0, int bi, int first = -1,
+                         int stride = kProducerThreads) {
       if constexpr (kBeta != Beta::kZero) {
         if (it.kb != 0) return;
         const int r1 = min(tm0 + P::kBM, p.m);
         const float *cbase = matrixC(bi);
 #pragma unroll 1
-        for (int cc = pt; cc < P::kBN; cc += kProducerThreads) {
+        for (int cc = first < 0 ? pt : first; cc < P::kBN; cc += stride) {
           const int col = tn0 + cc;
           if (col >= p.n) break;
           const float *colp = cbase + static_cast<size_t>(col) * p.ldc;
@@ -522,6 +531,51 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
                                                          k0, pt, p.b_vec);
             cpAsyncArrive(&full[s]);
           }
+        }
+      }
+    } else if (split_producer) {
+      // Transposing plans staged by TMA: warp 0 loads (lane 0 issues the
+      // TMA, its 32 lanes prefetch C), one item at a time; warps 1-3
+      // transpose every landed stage into the transposed ring. Deadlock-free:
+      // a load waits for the compute warps to release the stage it refills,
+      // a transpose for the stage to land and for the compute warps to
+      // release the buffer it overwrites, and the compute warps only for
+      // transposed buffers -- no role waits on one that waits on it.
+      if (pt < 32) {
+        int i = 0;   // iterations loaded so far, over all items
+        for (int idx = 0; idx < nitems; ++idx) {
+          const Item it = itemAt(p, cta, idx);
+          int m0, n0, bi;
+          origin(it.tile, &m0, &n0, &bi);
+          prefetchC(it, m0, n0, bi, pt, 32);
+          if (pt != 0) continue;
+#pragma unroll 1
+          for (int kt = it.kb; kt < it.ke; ++kt, ++i) {
+            const int s = i % kStages;
+            const int k0 = kt * kBK;
+            if (i >= kStages) {
+              wait(&empty[s], (i / kStages - 1) & 1);
+              fenceProxyAsyncShared();   // the compute warps read stage s with ld.shared
+            }
+            mbarArriveExpectTx(&full[s], kStageBytes);
+            if (P::kA == Layout::kXK) tmaLoad3d(stageA(s), &p.tma_a, &full[s], m0, k0, bi);
+            else tmaLoad3d(stageA(s), &p.tma_a, &full[s], k0, m0, bi);
+            if (P::kB == Layout::kXK) tmaLoad3d(stageB(s), &p.tma_b, &full[s], n0, k0, bi);
+            else tmaLoad3d(stageB(s), &p.tma_b, &full[s], k0, n0, bi);
+          }
+        }
+      } else {
+        const int xt = pt - 32;
+#pragma unroll 1
+        for (int j = 0; j < total; ++j) {
+          const int t = j % kTransBufs;
+          wait(&full[j % kStages], (j / kStages) & 1);
+          if (j >= kTransBufs) wait(&tempty[t], (j / kTransBufs - 1) & 1);
+          if constexpr (P::kTransP)
+            transposeKX<kBP, kTransposers>(stageP(j % kStages), tbufP(t), xt);
+          if constexpr (P::kTransD)
+            transposeKX<kBD, kTransposers>(stageD(j % kStages), tbufD(t), xt);
+          mbarArrive(&tfull[t]);
         }
       }
     } else {
