@@ -70,7 +70,7 @@ constexpr int kBlockThreads = kThreads + kProducerThreads;
 // With TMA staging and a transposed operand, warp 0 of the producer issues the
 // loads and the other three warps transpose.
 constexpr int kTransposers = kProducerThreads - 32;
-constexpr int kSplitMinIters = 24;
+constexpr int kSplitMinIters = 16;
 // Register split: the block is launched with kLaunchRegs per thread (what
 // __launch_bounds__(384, 1) leaves ptxas); setmaxnreg then moves registers
 // from the producer warpgroup to the compute warpgroups.
@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   const int tid = threadIdx.x;
   // Transposing plans staged by TMA split the producer into a loading warp
   // and three transposing warps when the CTA has enough iterations (measured:
-  // faster from 1024^3 up, slower for a single short piece, e.g. 768^3).
+  // faster from 896^3 up, slower for a single short piece, e.g. 768^3).
   const bool split_producer = P::kTrans && kSrc == Src::kTma && total >= kSplitMinIters;
 
   if (tid == 0) {
